@@ -1,0 +1,331 @@
+"""Benchmark of the Gemma 3 Q8_0 token loop on B200 (bs=1 greedy decode).
+
+Default workload: the 27B-shaped decoder (vocab
+262144, d 5376, 62 layers, 32 q / 16 KV heads of 128, ffn 21504, window 1024,
+5:1 local:global) with seeded synthetic Q8_0 weights generated on the device,
+a 2048-token seeded prompt prefilled token by token, then greedy decode.
+`--workload 270m` runs config 0's 270M shape instead.
+
+One step = one decoded token (batch 1).  Under torchrun (N > 1) the model is
+tensor-parallel over N GPUs (Q/K/V, gate, up column-sharded; o-proj, down
+row-sharded with an NCCL all-reduce; vocab-sharded LM head with an NCCL max
+of the argmax keys), so the N ranks decode the same tokens: value = tokens /
+max-over-ranks time ("scaling": "strong").
+
+Printed JSON line:
+  value          decode tok/s, K steps device-resident (graph replays, token fed
+                 back on the device), CUDA events on the model stream
+  e2e            tok/s through vrt_decode_step (the C ABI call a caller makes):
+                 host token + position copied in, argmax result copied out, per step
+  roofline       the dominant kernel (layer gate/up mat-vec: RMSNorm prologue,
+                 gelu*up epilogue) timed alone on the same stream; algorithmic
+                 bytes / time vs the measured HBM peak
+  cpu_baseline   the CPU oracle (C restatement of the reference token loop,
+                 GQA-generalised; the reference itself refuses head_count_kv != 1)
+                 on a bounded sample, extrapolated to one token
+  clocks         nvidia-smi samples taken during the timed region
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "vortex-rt_b200"), os.path.join(ROOT, "oracle")]
+
+import synth_gguf as sg  # noqa: E402
+
+PROMPT_LEN = {"27b": 2048, "270m": 8}
+METRIC = "decode tok/s (Gemma3-shaped Q8_0, bs=1 greedy)"
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic(workload: str):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(workload)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows: list[list[str]] = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def shape_for(workload: str) -> sg.Gemma3Shape:
+    return sg.SHAPES["27b" if workload == "27b" else "270m"]
+
+
+def bytes_per_token(shape: sg.Gemma3Shape, pos: int) -> int:
+    """Q8_0 weight bytes + norm vectors + embedding row + KV read/write at `pos`."""
+    d, hd = shape.embedding_length, shape.head_dim
+    q8 = lambda r, c: r * c // 32 * 34  # noqa: E731
+    layer = (q8(shape.q_width + 2 * shape.kv_width, d) + q8(d, shape.q_width) + 2 * q8(shape.feed_forward_length, d)
+             + q8(d, shape.feed_forward_length))
+    w = layer * shape.block_count + q8(shape.vocab_size, d)
+    norms = (4 * d + 2 * hd) * 4 * shape.block_count + 4 * d
+    kv = 0
+    for l in range(shape.block_count):
+        n = pos + 1 if (l + 1) % 6 == 0 else min(pos + 1, shape.sliding_window)
+        kv += n * shape.head_count_kv * hd * 4 * 2
+    return w + norms + d // 32 * 34 + kv
+
+
+def cpu_baseline(workload: str, threads: int) -> dict:
+    """Oracle port timed on a bounded sample of one decode token."""
+    import oracle as O
+
+    shape = shape_for(workload)
+    if workload == "270m":
+        sample_layers, sample_vocab = shape.block_count, shape.vocab_size
+    else:
+        sample_layers, sample_vocab = 2, 16384
+    small = shape.with_(block_count=sample_layers, vocab_size=sample_vocab)
+    o = O.Oracle(shape=small, seed=11, threads=threads, max_positions=8)
+    o.decode(2, 0, 1)  # warm caches / page in
+    o.reset()
+    t0 = time.perf_counter()
+    steps = 2
+    for p in range(steps):
+        o.decode(2 + p, p, 1)
+    t_tok = (time.perf_counter() - t0) / steps
+    # LM head slice alone, to split head vs layer time
+    raw = O.synth_q8(11, "token_embd.weight", sample_vocab, shape.embedding_length)
+    x = np.random.default_rng(0).standard_normal(shape.embedding_length).astype(np.float32)
+    t1 = time.perf_counter()
+    O.q8_matvec(raw, x, sample_vocab, lanes=64 if shape.embedding_length > 1024 else 8, threads=threads)
+    t_head = time.perf_counter() - t1
+    per_layer = max(t_tok - t_head, 1e-9) / sample_layers
+    full = per_layer * shape.block_count + t_head * (shape.vocab_size / sample_vocab)
+    o.close()
+    return {"value": 1.0 / full, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} decode tokens of a {sample_layers}-layer, {sample_vocab}-row-vocab slice of the "
+                      f"{workload} shape + one LM-head slice mat-vec, extrapolated to {shape.block_count} layers and "
+                      f"vocab {shape.vocab_size}; C restatement of src/gemma3.cpp (the reference itself refuses "
+                      f"head_count_kv != 1), {threads} host threads"}
+
+
+def run_reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(args.workload, threads)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(args.workload, threads))
+    v = statistics.median([x["value"] for x in vals])
+    cb = dict(vals[-1])
+    cb["value"] = v
+    shape = shape_for(args.workload)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "q8_0*f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}-shaped Gemma 3 Q8_0 decode, bs=1", "d_model": shape.embedding_length,
+                   "layers": shape.block_count, "vocab": shape.vocab_size},
+        "cpu_baseline": cb,
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="27b", choices=["27b", "270m"])
+    ap.add_argument("--prompt-len", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    import vrt
+
+    dist_on = world > 1
+    if dist_on:
+        torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    shape = shape_for(args.workload)
+    prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
+    e2e_steps = args.steps
+    positions = prompt_len + args.warmup + args.steps + e2e_steps + 8
+    prompt = [2] + np.random.default_rng(4).integers(3, shape.vocab_size, prompt_len - 1).tolist()
+
+    nccl_id = None
+    if dist_on:
+        obj = [vrt.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    ctx = vrt.Context(local)
+    cfg = vrt.Gemma3Config.from_shape(shape)
+    m = vrt.Model(ctx, None, config=cfg, seed=1234, max_positions=positions, tp_rank=rank, tp_world=world,
+                  nccl_id=nccl_id)
+    kernels = m.step_kernels()
+
+    def barrier():
+        if dist_on:
+            dist.barrier()
+
+    # prefill (token by token through the decode step, as the reference does)
+    t_pf = time.perf_counter()
+    m.prefill(prompt)
+    t_pf = time.perf_counter() - t_pf
+
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    # warmup
+    m.decode_steps_async(args.warmup)
+    ctx.sync()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ctx.sync()
+    barrier()
+    ev0.record(stream)
+    m.decode_steps_async(args.steps)
+    ev1.record(stream)
+    ctx.sync()
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist_on:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tok_s = args.steps / (ms / 1000.0)
+    status = m.device_status()
+    tok, pos = m.next_token()
+
+    # e2e through the C ABI call with host buffers (vrt_decode_step)
+    barrier()
+    ctx.sync()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        _, ids, _ = m.decode(tok, pos, 1, want_hidden=False)
+        tok, pos = int(ids[0]), pos + 1
+    ctx.sync()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if dist_on:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_tok_s = e2e_steps / float(te.item())
+
+    # dominant kernel alone: layer-0 gate/up mat-vec
+    k_ms, k_bytes = m.time_kernel(0, 2, iters=20)
+    peak, peak_kind = measured_peaks()
+    achieved = k_bytes / (k_ms / 1000.0) / 1e9
+    step_bytes = bytes_per_token(shape, prompt_len + args.warmup + args.steps // 2)
+    m.close()
+    ctx.close()
+
+    if rank == 0:
+        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, os.cpu_count() or 1)
+        tr = committed_traffic(args.workload)
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "q8_0*f32",
+            "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
+            "config": {"workload": f"config 4: {args.workload}-shaped Gemma 3 Q8_0, bs=1 greedy decode after a "
+                                   f"{prompt_len}-token prefill" if args.workload == "27b" else
+                                   f"config 0: 270M-shaped Gemma 3 Q8_0, bs=1 greedy decode after {prompt_len} "
+                                   "prompt tokens",
+                       "d_model": shape.embedding_length, "layers": shape.block_count,
+                       "heads": f"{shape.head_count}q/{shape.head_count_kv}kv x {shape.head_dim}",
+                       "ffn": shape.feed_forward_length, "vocab": shape.vocab_size, "global_batch": 1,
+                       "positions": f"{prompt_len + args.warmup}..{prompt_len + args.warmup + args.steps}",
+                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB streamed per token)"},
+            "gpu_launches": kernels * args.steps,
+            "kernels_per_step": kernels,
+            "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * tok_s / 1e9 / world,
+                              "peak_gbs": peak, "frac": step_bytes * tok_s / 1e9 / world / peak,
+                              "note": "per GPU; weights + norms + KV per token over device time"},
+            "roofline": {"bound": "hbm", "kernel": "q8t_gemv_kernel<Resid, GeluPair> (layer gate/up)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": k_bytes,
+                         "ms_per_launch": k_ms, "traffic": tr},
+            "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 40},
+            "prefill_s": t_pf,
+            "device_status": status,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

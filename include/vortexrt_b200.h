@@ -1,0 +1,254 @@
+/*
+ * vortexrt_b200.h -- C ABI of the B200 (sm_100a) backend for the Vortex-RT
+ * Gemma 3 Q8_0 token loop.
+ *
+ * Every entry point returns 0 on success or a negative VRT_E_* code; the
+ * message of the last failure on the calling thread is vrt_last_error().  No
+ * C++ exception crosses this boundary.  Pointers named d_* are device
+ * pointers, h_* host pointers.  `stream` is a cudaStream_t passed as void*
+ * (NULL = the context's own stream).  Sizes are bytes unless named *_dim or
+ * *_count.
+ *
+ * Each function cites the reference interface it replaces (paths inside the
+ * Vortex-RT tree).  The reference's Vulkan layer (vulkan_context, buffer,
+ * compute_pipeline) maps onto vrt_ctx_* / vrt_alloc / vrt_upload*; its
+ * pipelines (Q8MatVecPipeline, ArgmaxPipeline) onto vrt_q8_* / vrt_argmax;
+ * Gemma3Model onto vrt_model_*.
+ */
+#ifndef VORTEXRT_B200_H
+#define VORTEXRT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VRT_API __attribute__((visibility("default")))
+
+enum {
+    VRT_OK = 0,
+    VRT_E_INVALID = -1,   /* bad argument, shape, alignment or range        */
+    VRT_E_CUDA = -2,      /* a CUDA runtime call failed                     */
+    VRT_E_NOMEM = -3,     /* device or host allocation failed               */
+    VRT_E_IO = -4,        /* file open / read / GGUF parse failure          */
+    VRT_E_STATE = -5,     /* call order (positions, uninitialised model)    */
+    VRT_E_NUMERIC = -6,   /* non-finite hidden state or invalid argmax      */
+    VRT_E_TIMEOUT = -7,   /* a bounded device-side wait gave up             */
+    VRT_E_UNSUPPORTED = -8
+};
+
+typedef struct vrt_ctx vrt_ctx;
+typedef struct vrt_model vrt_model;
+
+/* Result of an argmax: same layout as vortexrt::ArgmaxResult (include/vortexrt/argmax.hpp:12-17). */
+typedef struct {
+    uint32_t index;
+    float value;
+} vrt_argmax_result;
+
+typedef struct {
+    char name[256];
+    int device;
+    int sm_count;
+    int cc_major, cc_minor;
+    uint32_t warp_size;       /* reported where the reference reported subgroup_size */
+    uint64_t global_mem_bytes;
+    uint64_t l2_bytes;
+} vrt_device_info;
+
+/* ------------------------------------------------------------ runtime */
+
+/* Thread-local message of the last failed call ("" if none). */
+VRT_API const char* vrt_last_error(void);
+VRT_API const char* vrt_version(void);
+
+/* Open device `device` (-1 = VORTEXRT_DEVICE env var, else 0).
+ * Replaces VulkanContext(device_selector) (src/vulkan_context.cpp:116-144). */
+VRT_API int vrt_ctx_create(int device, vrt_ctx** out);
+VRT_API int vrt_ctx_destroy(vrt_ctx* ctx);
+/* Replaces VulkanContext::capabilities() (include/vortexrt/vulkan_context.hpp:56). */
+VRT_API int vrt_ctx_info(vrt_ctx* ctx, vrt_device_info* out);
+VRT_API int vrt_ctx_synchronize(vrt_ctx* ctx);
+/* The context's stream (cudaStream_t). */
+VRT_API void* vrt_ctx_stream(vrt_ctx* ctx);
+
+/* Device allocation, 256-byte aligned, zero-filled, with 256 bytes of tail padding.
+ * Replaces Buffer(ctx, size, usage, props) / ~Buffer (src/buffer.cpp:11-79). */
+VRT_API int vrt_alloc(vrt_ctx* ctx, size_t bytes, void** d_out);
+VRT_API int vrt_free(vrt_ctx* ctx, void* d_ptr);
+/* Synchronous copies.  Replace Buffer::upload / Buffer::download (src/buffer.cpp:81-197). */
+VRT_API int vrt_upload(vrt_ctx* ctx, void* d_dst, const void* h_src, size_t bytes);
+VRT_API int vrt_download(vrt_ctx* ctx, void* h_dst, const void* d_src, size_t bytes);
+/* Asynchronous copies on `stream` (host memory should be pinned for overlap). */
+VRT_API int vrt_upload_async(vrt_ctx* ctx, void* d_dst, const void* h_src, size_t bytes, void* stream);
+VRT_API int vrt_download_async(vrt_ctx* ctx, void* h_dst, const void* d_src, size_t bytes, void* stream);
+VRT_API int vrt_host_alloc_pinned(size_t bytes, void** h_out);
+VRT_API int vrt_host_free_pinned(void* h_ptr);
+
+/* ---------------------------------------------- Q8_0 pipeline kernels
+ * Weights are raw GGUF Q8_0 rows (34-byte blocks: fp16 scale + 32 int8) in a
+ * device buffer of `weights_bytes`, at `weight_byte_offset` (4-byte aligned).
+ * input_dim % 32 == 0.  Results are fp32.  Asynchronous on `stream`.
+ * Accumulation: int8 weights x int16-quantised activation blocks, exact
+ * integer block sums, fp32 across blocks. */
+
+/* y[output_dim] = W x.  Replaces Q8MatVecPipeline::run (src/q8_matvec.cpp:801-930). */
+VRT_API int vrt_q8_gemv(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes,
+                        uint64_t weight_byte_offset, const float* d_x, float* d_y,
+                        uint32_t input_dim, uint32_t output_dim, void* stream);
+
+/* `count` (1..8) mat-vecs sharing x; outputs packed back to back in d_y
+ * (matrix i at element sum(output_dims[0..i))).  Replaces
+ * Q8MatVecPipeline::run_staged_pair / run_staged_triplet (src/q8_matvec.cpp:2007-2890). */
+VRT_API int vrt_q8_gemv_multi(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes,
+                              const uint64_t* weight_byte_offsets, const uint32_t* output_dims,
+                              uint32_t count, const float* d_x, float* d_y, uint32_t input_dim,
+                              void* stream);
+
+/* y = W_down (gelu_tanh(W_gate x) * (W_up x)).  d_workspace holds 2*ffn_dim floats.
+ * Replaces Q8MatVecPipeline::run_staged_ffn (src/q8_matvec.cpp:1360-2004). */
+VRT_API int vrt_q8_ffn(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes,
+                       uint64_t gate_off, uint64_t up_off, uint64_t down_off, const float* d_x,
+                       float* d_workspace, float* d_y, uint32_t input_dim, uint32_t ffn_dim,
+                       uint32_t output_dim, void* stream);
+
+/* gate[i] = gelu_tanh(gate[i]) * up[i].  Replaces shaders/gelu_mul.comp. */
+VRT_API int vrt_gelu_mul(vrt_ctx* ctx, float* d_gate, const float* d_up, uint32_t count, void* stream);
+
+/* argmax over count floats: ties -> lower index, NaN never wins; all-NaN gives
+ * {0xffffffff, -inf}.  Replaces ArgmaxPipeline::run (src/argmax.cpp:503-567). */
+VRT_API int vrt_argmax(vrt_ctx* ctx, const float* d_x, uint32_t count, vrt_argmax_result* d_out,
+                       void* stream);
+
+/* Tied LM head fused with argmax: the logits never reach memory unless
+ * d_logits != NULL.  Replaces run_q8_matvec_to_output + ArgmaxPipeline::run
+ * (src/gemma3.cpp:1146-1185). */
+VRT_API int vrt_lm_head_argmax(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes,
+                               uint64_t weight_byte_offset, const float* d_x, uint32_t input_dim,
+                               uint32_t vocab, float* d_logits, vrt_argmax_result* d_out,
+                               void* stream);
+
+/* --------------------------------------- packed (Q8T) fast path
+ * The model's own weight layout, exposed for callers that keep a matrix
+ * resident and call it many times: rows of 16 x 128-column tiles, each tile's
+ * bytes in the order one warp consumes them (same 34 bytes per 32 weights as
+ * GGUF).  cols % 128 == 0.  Tiled mat-vecs stream the weights with bulk
+ * copies through shared memory.  No reference counterpart: these are the
+ * kernels behind vrt_model_* made callable on their own. */
+
+VRT_API uint64_t vrt_q8t_bytes(uint32_t rows, uint32_t cols);
+/* Repack `rows` raw Q8_0 rows at byte `offset` of d_raw into d_packed (vrt_q8t_bytes(rows, cols) bytes). */
+VRT_API int vrt_q8t_pack(vrt_ctx* ctx, const void* d_raw, uint64_t raw_bytes, uint64_t offset, uint32_t rows,
+                         uint32_t cols, void* d_packed, void* stream);
+/* Interleave gate and up matrices (ffn rows each) into one packed pair (vrt_q8t_bytes(2*ffn, cols)). */
+VRT_API int vrt_q8t_pack_pair(vrt_ctx* ctx, const void* d_raw, uint64_t raw_bytes, uint64_t gate_offset,
+                              uint64_t up_offset, uint32_t ffn, uint32_t cols, void* d_packed, void* stream);
+/* y = W x with W packed. */
+VRT_API int vrt_q8t_gemv(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint32_t cols, const float* d_x,
+                         float* d_y, void* stream);
+/* act = gelu_tanh(W_gate x) * (W_up x), one kernel over a packed pair. */
+VRT_API int vrt_q8t_gate_up(vrt_ctx* ctx, const void* d_packed_pair, uint32_t ffn, uint32_t cols,
+                            const float* d_x, float* d_act, void* stream);
+/* Fused FFN over packed weights: two kernels (gate/up + gelu, down). */
+VRT_API int vrt_q8t_ffn(vrt_ctx* ctx, const void* d_gate_up, const void* d_down, uint32_t input_dim,
+                        uint32_t ffn_dim, uint32_t output_dim, const float* d_x, float* d_act, float* d_y,
+                        void* stream);
+/* LM head + argmax over a packed vocab matrix (logits written when d_logits != NULL). */
+VRT_API int vrt_q8t_lm_head_argmax(vrt_ctx* ctx, const void* d_packed, uint32_t vocab, uint32_t cols,
+                                   const float* d_x, float* d_logits, vrt_argmax_result* d_out, void* stream);
+
+/* ------------------------------------------------------------ model */
+
+typedef struct {
+    uint32_t context_length, embedding_length, block_count, feed_forward_length;
+    uint32_t head_count, head_count_kv, head_dim, value_dim, vocab_size, sliding_window;
+    float rms_epsilon, global_rope_base, local_rope_base;
+} vrt_gemma3_config; /* = vortexrt::Gemma3Config (include/vortexrt/gemma3.hpp:19-33) */
+
+typedef struct {
+    uint32_t max_positions; /* KV/rope capacity; 0 = min(context_length, 8192) */
+    int tp_rank;            /* tensor-parallel rank (0 when tp_world <= 1)      */
+    int tp_world;           /* tensor-parallel width (0/1 = single GPU)         */
+    const void* nccl_id;    /* ncclUniqueId bytes when tp_world > 1             */
+    int use_graph;          /* capture the decode step in a CUDA graph          */
+    int use_pdl;            /* programmatic dependent launch between kernels    */
+} vrt_model_options;
+
+/* Defaults: max_positions 0, single GPU, use_graph = 1, use_pdl = 1. */
+VRT_API void vrt_model_options_default(vrt_model_options* o);
+
+/* Load a Gemma 3 Q8_0 GGUF: weights repacked into the device arena, norms,
+ * rope tables and KV cache allocated.  Replaces the Gemma3Model constructor
+ * (src/gemma3.cpp:72-654); lifts its one-KV-head and 4 GiB limits. */
+VRT_API int vrt_model_load(vrt_ctx* ctx, const char* gguf_path, const vrt_model_options* opts,
+                           vrt_model** out);
+
+/* Build the seeded synthetic model of the given shape directly in device
+ * memory (the generator of synth_gguf.py, bit-identical to loading the file
+ * it writes).  For benchmarks of shapes too large to write as files. */
+VRT_API int vrt_model_create_synthetic(vrt_ctx* ctx, const vrt_gemma3_config* cfg, uint64_t seed,
+                                       const vrt_model_options* opts, vrt_model** out);
+VRT_API int vrt_model_destroy(vrt_model* m);
+VRT_API int vrt_model_config(vrt_model* m, vrt_gemma3_config* out);
+
+/* Gemma3Model::reset_cache (src/gemma3.cpp:1454-1460). */
+VRT_API int vrt_model_reset(vrt_model* m);
+
+/* Gemma3Model::decode_token (src/gemma3.cpp:1462-1882).  position must equal
+ * the next position.  top_k == 0 skips the LM head; 1 = fused LM head +
+ * argmax; >1 = full logits, top-k by value.  h_hidden (optional) receives the
+ * final normed hidden state (embedding_length floats); h_ids/h_logits receive
+ * min(top_k, vocab) entries. */
+VRT_API int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t top_k,
+                            float* h_hidden, uint32_t* h_ids, float* h_logits);
+
+/* Full-vocabulary logits of the last decode step into h_logits (vocab floats). */
+VRT_API int vrt_model_logits(vrt_model* m, float* h_logits);
+
+/* Gemma3Model::generate_greedy_tokens (src/gemma3.cpp:2080-2149): token-by-token
+ * prefill, greedy decode until max_new tokens or EOS.  Runs on the device with
+ * no host round trip per token; h_out receives *h_count <= max_new ids. */
+VRT_API int vrt_generate_greedy(vrt_model* m, const uint32_t* h_prompt, uint32_t prompt_count,
+                                uint32_t max_new, uint32_t* h_out, uint32_t* h_count);
+
+/* Device-resident continuation for benchmarks: runs `steps` greedy decode steps
+ * from the current state (after a prefill), the i-th generated id written to
+ * d_out_ids[i] when non-NULL.  No host synchronisation. */
+VRT_API int vrt_decode_steps_async(vrt_model* m, uint32_t steps, uint32_t* d_out_ids, void* stream);
+
+/* Prefill helper: feeds prompt tokens through the decode step without the LM
+ * head (the reference's top_k = 0 prompt steps) except the last one.  After it
+ * the model holds the argmax of the last prompt token as its next input. */
+VRT_API int vrt_prefill(vrt_model* m, const uint32_t* h_prompt, uint32_t prompt_count);
+
+/* Greedy token that the next vrt_decode_steps_async step will consume. */
+VRT_API int vrt_model_next_token(vrt_model* m, uint32_t* h_token, uint32_t* h_position);
+
+/* Number of kernels one decode step launches (graph nodes), for reporting. */
+VRT_API int vrt_model_step_kernels(vrt_model* m, uint32_t* out);
+
+/* Device error word (bounded waits that gave up, invalid tokens) and clear it. */
+VRT_API int vrt_model_device_status(vrt_model* m, uint32_t* h_status);
+
+/* Per-layer residual trace of the last decode step (block_count x d floats),
+ * for debugging against the CPU oracle.  Enabled by vrt_model_set_trace(m, 1). */
+VRT_API int vrt_model_set_trace(vrt_model* m, int enabled);
+VRT_API int vrt_model_trace(vrt_model* m, float* h_out);
+
+/* Benchmark helper: average device time of one of the decode step's
+ * mat-vec launches run alone (0 qkv, 1 o-proj, 2 gate/up, 3 down, 4 LM head
+ * of `layer`), and its algorithmic bytes (weights + vectors once).  Clobbers
+ * activations; call vrt_model_reset before decoding again. */
+VRT_API int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, uint32_t iters,
+                                  float* ms_per_launch, uint64_t* algorithmic_bytes);
+
+/* NCCL unique id for tensor parallelism (128 bytes). */
+VRT_API int vrt_tp_unique_id(void* h_out128);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VORTEXRT_B200_H */

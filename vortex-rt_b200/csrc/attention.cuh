@@ -1,0 +1,244 @@
+// Decode attention for one layer, one token (src/gemma3.cpp:1557-1696 plus
+// the KV push of 1590-1600), split over the key history:
+//   grid = (splits, kv_heads), 128 threads.  CTA (s, g) serves the R = H/KV
+//   query heads of KV head g over its share of the history.
+//   1. q heads -> per-head RMSNorm (fp64 sum of squares) -> NeoX RoPE with
+//      the position's cos/sin row, in registers (lane l holds dims l + 32m,
+//      so both halves of every rotated pair sit in the same lane).
+//   2. The CTA holding the newest position builds k (RMSNorm + RoPE) and v
+//      for it, writes them to the cache slot (position % capacity: a ring of
+//      `window` slots for sliding layers, linear for global ones) and uses
+//      them from shared memory; no CTA reads a slot another CTA writes.
+//   3. Each warp walks positions with an online softmax; the CTA merges its
+//      warps and stores (max, sum, acc) per head to the split scratch.
+//   4. The last CTA of the KV head (atomic ticket) merges the splits in split
+//      order (deterministic) and writes the attention output, fp32.
+#pragma once
+
+#include "vrt_device.cuh"
+
+namespace vrt {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kMaxGroup = 8;   // query heads per KV head handled by one CTA
+
+struct AttnParams {
+    const float* qkv;       // q [H*hd] | k [KV*hd] | v [KV*hd]
+    const float* q_norm;    // [hd]
+    const float* k_norm;    // [hd]
+    const float* rope_cos;  // [positions][hd/2]
+    const float* rope_sin;
+    float* k_cache;         // [KV][cap][hd]
+    float* v_cache;
+    uint32_t cap;
+    uint32_t window;        // 0 for global layers
+    const uint32_t* pos;    // device position
+    uint32_t H, KV, hd;
+    float eps, scale;
+    float* part_ml;         // [H][splits][2]
+    float* part_acc;        // [H][splits][hd]
+    uint32_t* tickets;      // [KV]
+    float* out;             // [H*hd]
+    uint32_t splits;
+    float* zero0;           // buffer this launch clears
+    uint32_t zero0_count;
+};
+
+template <int M>  // M = hd / 32 values per lane
+__device__ __forceinline__ void head_norm_rope(float (&v)[M], const float* w, const float* cs, const float* sn,
+                                               uint32_t hd, float eps, int lane) {
+    double ss = 0.0;
+#pragma unroll
+    for (int m = 0; m < M; ++m) ss += static_cast<double>(v[m]) * static_cast<double>(v[m]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(hd)) + eps);
+#pragma unroll
+    for (int m = 0; m < M; ++m) v[m] = __fmul_rn(v[m], __fmul_rn(scale, w[lane + 32 * m]));
+#pragma unroll
+    for (int m = 0; m < M / 2; ++m) {
+        const uint32_t i = lane + 32 * m;
+        const float c = cs[i], s = sn[i];
+        const float a = v[m], b = v[m + M / 2];
+        v[m] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        v[m + M / 2] = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    }
+}
+
+// M = head_dim / 32, RG >= H / KV (1, 2, 4 or 8).
+template <int M, int RG>
+__global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
+    constexpr int HD = M * 32;
+    __shared__ float q_s[RG][HD];
+    __shared__ float knew[HD], vnew[HD];
+    __shared__ float w_ml[kAttnWarps][RG][2];
+    __shared__ float w_acc[kAttnWarps][RG][HD];
+    __shared__ uint32_t last_flag;
+
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t g = blockIdx.y, s = blockIdx.x;
+    const uint32_t R = p.H / p.KV, hd = p.hd;
+    if (p.zero0) {
+        const uint32_t nb = gridDim.x * gridDim.y, b = blockIdx.y * gridDim.x + blockIdx.x;
+        const uint32_t a0 = static_cast<uint64_t>(p.zero0_count) * b / nb;
+        const uint32_t a1 = static_cast<uint64_t>(p.zero0_count) * (b + 1) / nb;
+        for (uint32_t i = a0 + tid; i < a1; i += kAttnThreads) p.zero0[i] = 0.0f;
+    }
+    const uint32_t pos = *p.pos;
+    const uint32_t n = p.window ? min(pos + 1, p.window) : pos + 1;
+    const uint32_t first = pos + 1 - n;  // oldest position attended
+    const uint32_t chunk = (n + p.splits - 1) / p.splits;
+    const uint32_t t0 = first + s * chunk;
+    const uint32_t t1 = min(first + n, t0 + chunk);
+    const float* cs = p.rope_cos + static_cast<uint64_t>(pos) * (hd / 2);
+    const float* sn = p.rope_sin + static_cast<uint64_t>(pos) * (hd / 2);
+
+    // 1. queries
+    for (uint32_t r = warp; r < R; r += kAttnWarps) {
+        const float* src = p.qkv + static_cast<uint64_t>(g * R + r) * hd;
+        float v[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) v[m] = src[lane + 32 * m];
+        head_norm_rope<M>(v, p.q_norm, cs, sn, hd, p.eps, lane);
+#pragma unroll
+        for (int m = 0; m < M; ++m) q_s[r][lane + 32 * m] = v[m];
+    }
+    // 2. the newest key/value
+    const bool has_new = t0 < t1 && t1 == pos + 1;
+    if (has_new && warp == 0) {
+        const float* ks = p.qkv + static_cast<uint64_t>(p.H) * hd + static_cast<uint64_t>(g) * hd;
+        const float* vs = p.qkv + static_cast<uint64_t>(p.H + p.KV) * hd + static_cast<uint64_t>(g) * hd;
+        float v[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) v[m] = ks[lane + 32 * m];
+        head_norm_rope<M>(v, p.k_norm, cs, sn, hd, p.eps, lane);
+        const uint32_t slot = pos % p.cap;
+        float* kd = p.k_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
+        float* vd = p.v_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const float vv = vs[lane + 32 * m];
+            knew[lane + 32 * m] = v[m];
+            vnew[lane + 32 * m] = vv;
+            kd[lane + 32 * m] = v[m];
+            vd[lane + 32 * m] = vv;
+        }
+    }
+    __syncthreads();
+
+    // 3. online softmax over this CTA's positions
+    float mx[RG], sm[RG], acc[RG][M];
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+        mx[r] = -INFINITY;
+        sm[r] = 0.0f;
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
+    }
+    for (uint32_t t = t0 + warp; t < t1; t += kAttnWarps) {
+        float kv[M], vv[M];
+        if (t == pos) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                kv[m] = knew[lane + 32 * m];
+                vv[m] = vnew[lane + 32 * m];
+            }
+        } else {
+            const uint64_t base = (static_cast<uint64_t>(g) * p.cap + (t % p.cap)) * hd;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                kv[m] = __ldcg(p.k_cache + base + lane + 32 * m);
+                vv[m] = __ldcg(p.v_cache + base + lane + 32 * m);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+            if (r < static_cast<int>(R)) {
+                float d = 0.0f;
+#pragma unroll
+                for (int m = 0; m < M; ++m) d = fmaf(q_s[r][lane + 32 * m], kv[m], d);
+                d = warp_sum(d);
+                const float sc = d * p.scale;
+                const float nm = fmaxf(mx[r], sc);
+                const float corr = expf(mx[r] - nm);
+                const float pr = expf(sc - nm);
+                sm[r] = sm[r] * corr + pr;
+#pragma unroll
+                for (int m = 0; m < M; ++m) acc[r][m] = fmaf(pr, vv[m], acc[r][m] * corr);
+                mx[r] = nm;
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+        if (r < static_cast<int>(R)) {
+            if (lane == 0) {
+                w_ml[warp][r][0] = mx[r];
+                w_ml[warp][r][1] = sm[r];
+            }
+#pragma unroll
+            for (int m = 0; m < M; ++m) w_acc[warp][r][lane + 32 * m] = acc[r][m];
+        }
+    }
+    __syncthreads();
+    // merge warps -> split partial
+    for (uint32_t r = warp; r < R; r += kAttnWarps) {
+        float M_ = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) M_ = fmaxf(M_, w_ml[w][r][0]);
+        float L_ = 0.0f;
+        float a[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) a[m] = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = (M_ == -INFINITY) ? 0.0f : expf(w_ml[w][r][0] - M_);
+            L_ += w_ml[w][r][1] * f;
+#pragma unroll
+            for (int m = 0; m < M; ++m) a[m] = fmaf(w_acc[w][r][lane + 32 * m], f, a[m]);
+        }
+        const uint32_t h = g * R + r;
+        float* pa = p.part_acc + (static_cast<uint64_t>(h) * p.splits + s) * hd;
+#pragma unroll
+        for (int m = 0; m < M; ++m) pa[lane + 32 * m] = a[m];
+        if (lane == 0) {
+            p.part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2] = M_;
+            p.part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2 + 1] = L_;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t ticket = atomicAdd(p.tickets + g, 1u);
+        last_flag = (ticket == p.splits - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    // 4. merge splits in order
+    for (uint32_t r = warp; r < R; r += kAttnWarps) {
+        const uint32_t h = g * R + r;
+        const float* ml = p.part_ml + static_cast<uint64_t>(h) * p.splits * 2;
+        float M_ = -INFINITY;
+        for (uint32_t q = 0; q < p.splits; ++q) M_ = fmaxf(M_, __ldcg(ml + 2 * q));
+        float L_ = 0.0f, a[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) a[m] = 0.0f;
+        for (uint32_t q = 0; q < p.splits; ++q) {
+            const float mq = __ldcg(ml + 2 * q);
+            if (mq == -INFINITY) continue;
+            const float f = expf(mq - M_);
+            L_ += __ldcg(ml + 2 * q + 1) * f;
+            const float* pa = p.part_acc + (static_cast<uint64_t>(h) * p.splits + q) * hd;
+#pragma unroll
+            for (int m = 0; m < M; ++m) a[m] = fmaf(__ldcg(pa + lane + 32 * m), f, a[m]);
+        }
+        const float inv = 1.0f / L_;
+#pragma unroll
+        for (int m = 0; m < M; ++m) p.out[static_cast<uint64_t>(h) * hd + lane + 32 * m] = a[m] * inv;
+    }
+    if (tid == 0) p.tickets[g] = 0u;
+}
+
+}  // namespace vrt

@@ -1,0 +1,380 @@
+// Q8_0 x fp32 mat-vec over the tiled (Q8T) weight layout, sm_100a.
+//
+// One persistent CTA per SM owns a contiguous span of weight tiles.  Warp 8
+// (the producer) streams the span through a 4-stage shared-memory ring with
+// 1-D bulk copies (cp.async.bulk ... mbarrier::complete_tx), starting before
+// griddepcontrol.wait so the weight stream overlaps the previous kernel's
+// tail.  Warps 0-7 (consumers) first build the activation vector (the
+// prologue: plain copy, RMSNorm, embedding + RMSNorm or residual + two
+// RMSNorms, all with fp64 sums of squares like src/gemma3.cpp:948-1104),
+// quantise it to int16 per 32-block, then each consumes one tile per stage:
+// 16 dp2a per row pair give exact integer block sums, which are scaled by
+// the weight's fp16 block scale and the activation block scale and summed in
+// fp32.  Row results are reduced across lanes and warps in a fixed order
+// (deterministic, replay-identical) and go to one of three epilogues:
+//   Atomic   : y[row] += v into a zeroed buffer.  The span is tile-granular,
+//              so at most two CTAs touch a row and the sum is order-free.
+//   GeluPair : rows come as 8 gate + 8 up per group; act = gelu(g) * u.
+//   Argmax   : logits (optional) + a 64-bit atomicMax key (ties -> lower
+//              index, NaN skipped), the fused tied LM head + argmax.
+#pragma once
+
+#include "vrt_device.cuh"
+
+namespace vrt {
+
+enum Pro : int { kProPlain = 0, kProRmsInto = 1, kProEmbed = 2, kProResid = 3, kProResidFinal = 4 };
+enum Epi : int { kEpiAtomic = 0, kEpiGeluPair = 1, kEpiArgmax = 2 };
+
+struct GemvParams {
+    const uint8_t* w;      // tiled matrix
+    uint32_t rows;         // output rows of the tiled matrix (GeluPair: 2 * ffn)
+    uint32_t cols;         // K, multiple of 128
+    const float* x;        // Plain: activations; RmsInto: residual; Resid*: block output to post-norm
+    const float* h_prev;   // Resid*: residual stream in
+    const float* w_post;   // Resid*: post-norm weight
+    const float* w_pre;    // RmsInto/Embed/Resid: pre-norm weight; ResidFinal: output norm
+    float* h_out;          // Embed/Resid: new residual (CTA 0); ResidFinal: normed hidden (CTA 0)
+    float* trace;          // Resid*: optional copy of the new residual (CTA 0)
+    const uint8_t* embd;   // Embed: tiled token_embd (cols = K)
+    const uint32_t* token; // Embed: device token id
+    uint32_t vocab;
+    float emb_scale;
+    float eps;
+    float* y;                    // Atomic: output; GeluPair: act; Argmax: logits or null
+    unsigned long long* amax;    // Argmax key
+    uint32_t row_base;           // Argmax: global index of local row 0 (vocab shard)
+    uint32_t* status;
+    float* zero0;                // buffers this launch clears after griddepcontrol.wait
+    uint32_t zero0_count;
+    float* zero1;
+    uint32_t zero1_count;
+};
+
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStageTiles = kConsumerWarps;
+constexpr int kStageBytes = kStageTiles * kTileBytes;  // 17408
+constexpr int kStages = 4;
+constexpr int kChunkGroups = 8;                        // rows reduced per chunk barrier = 128
+
+struct GemvSmem {
+    // byte offsets inside dynamic shared memory
+    uint32_t stages, bars, partial, red, sx, x16, xs, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(uint32_t cols, int pro) {
+    GemvSmem s;
+    s.stages = 0;
+    s.bars = s.stages + kStages * kStageBytes;
+    s.partial = s.bars + 2 * kStages * 8;
+    s.red = s.partial + 2 * kConsumerWarps * kChunkGroups * 16 * 4;
+    s.sx = s.red + 64 * 8;
+    s.x16 = (s.sx + (cols / 32) * 4 + 15) / 16 * 16;
+    s.xs = (s.x16 + cols * 2 + 15) / 16 * 16;
+    s.total = s.xs + ((pro == kProPlain || pro == kProRmsInto) ? 0u : cols * 4u);
+    return s;
+}
+
+__device__ __forceinline__ int dot16(const uint4 w, const uint4 xl, const uint4 xh, int acc) {
+    acc = __dp2a_lo(static_cast<int>(xl.x), static_cast<int>(w.x), acc);
+    acc = __dp2a_hi(static_cast<int>(xl.y), static_cast<int>(w.x), acc);
+    acc = __dp2a_lo(static_cast<int>(xl.z), static_cast<int>(w.y), acc);
+    acc = __dp2a_hi(static_cast<int>(xl.w), static_cast<int>(w.y), acc);
+    acc = __dp2a_lo(static_cast<int>(xh.x), static_cast<int>(w.z), acc);
+    acc = __dp2a_hi(static_cast<int>(xh.y), static_cast<int>(w.z), acc);
+    acc = __dp2a_lo(static_cast<int>(xh.z), static_cast<int>(w.w), acc);
+    acc = __dp2a_hi(static_cast<int>(xh.w), static_cast<int>(w.w), acc);
+    return acc;
+}
+
+// Sum over the 256 consumer threads in fp64, fixed order; result broadcast.
+__device__ __forceinline__ double consumer_sum(double v, double* red) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    named_bar_sync(1, kConsumerWarps * 32);
+    double s = 0.0;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) s += red[w];
+    named_bar_sync(1, kConsumerWarps * 32);
+    return s;
+}
+
+// Quantise 32 consecutive activations (block `blk`) into the permuted int16
+// layout + scale.
+__device__ __forceinline__ void quant_block(const float* v, uint32_t blk, int16_t* x16p, float* sx) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    const float s = quant_scale(amax);
+    const float inv = amax > 0.0f ? 32767.0f / amax : 0.0f;
+    sx[blk] = s;
+    const uint32_t base = (blk / 4) * 128 + (blk % 4) * 8;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int q0 = quant_one(v[p * 8 + 2 * e], inv), q1 = quant_one(v[p * 8 + 2 * e + 1], inv);
+            wv[e] = (static_cast<uint32_t>(q0) & 0xffffu) | (static_cast<uint32_t>(q1) << 16);
+        }
+        *reinterpret_cast<uint4*>(x16p + base + p * 32) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvSmem L = gemv_smem_layout(p.cols, PRO);
+    uint8_t* stages = smem + L.stages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+    uint64_t* empty = full + kStages;
+    float* partial = reinterpret_cast<float*>(smem + L.partial);
+    double* red = reinterpret_cast<double*>(smem + L.red);
+    float* sx = reinterpret_cast<float*>(smem + L.sx);
+    int16_t* x16p = reinterpret_cast<int16_t*>(smem + L.x16);
+    float* xs = reinterpret_cast<float*>(smem + L.xs);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t kt = p.cols / kTileCols;
+    const uint32_t n_groups = (p.rows + kTileRows - 1) / kTileRows;
+    uint64_t T0, T1;
+    if (EPI == kEpiAtomic) {
+        const uint64_t total = static_cast<uint64_t>(n_groups) * kt;
+        T0 = total * blockIdx.x / gridDim.x;
+        T1 = total * (blockIdx.x + 1) / gridDim.x;
+    } else {
+        T0 = static_cast<uint64_t>(n_groups) * blockIdx.x / gridDim.x * kt;
+        T1 = static_cast<uint64_t>(n_groups) * (blockIdx.x + 1) / gridDim.x * kt;
+    }
+    const uint32_t n_tiles = static_cast<uint32_t>(T1 - T0);
+    const uint32_t n_stages = (n_tiles + kStageTiles - 1) / kStageTiles;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == kConsumerWarps) {
+        // ----------------------------------------------------- producer
+        if (lane == 0) {
+            const uint8_t* src = p.w + T0 * kTileBytes;
+            for (uint32_t st = 0; st < n_stages; ++st) {
+                const uint32_t s = st % kStages, r = st / kStages;
+                if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1)) atomicOr(p.status, kStatusWaitTimeout);
+                const uint32_t tiles = min(static_cast<uint32_t>(kStageTiles), n_tiles - st * kStageTiles);
+                const uint32_t bytes = tiles * kTileBytes;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_copy_g2s(stages + s * kStageBytes, src + static_cast<uint64_t>(st) * kStageBytes, bytes, &full[s]);
+            }
+        }
+        return;
+    }
+
+    // --------------------------------------------------------- consumers
+    pdl_wait();
+    const int ctid = tid;  // 0..255
+    constexpr int NC = kConsumerWarps * 32;
+    if (p.zero0) {
+        const uint32_t a = static_cast<uint64_t>(p.zero0_count) * blockIdx.x / gridDim.x;
+        const uint32_t b = static_cast<uint64_t>(p.zero0_count) * (blockIdx.x + 1) / gridDim.x;
+        for (uint32_t i = a + ctid; i < b; i += NC) p.zero0[i] = 0.0f;
+    }
+    if (p.zero1) {
+        const uint32_t a = static_cast<uint64_t>(p.zero1_count) * blockIdx.x / gridDim.x;
+        const uint32_t b = static_cast<uint64_t>(p.zero1_count) * (blockIdx.x + 1) / gridDim.x;
+        for (uint32_t i = a + ctid; i < b; i += NC) p.zero1[i] = 0.0f;
+    }
+    for (int i = ctid; i < 2 * kConsumerWarps * kChunkGroups * 16; i += NC) partial[i] = 0.0f;
+
+    const uint32_t K = p.cols, nblk = K / 32;
+    if (PRO == kProPlain) {
+        for (uint32_t blk = ctid; blk < nblk; blk += NC) {
+            float v[32];
+            const float4* src = reinterpret_cast<const float4*>(p.x + blk * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 f = src[q];
+                v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+            }
+            quant_block(v, blk, x16p, sx);
+        }
+    } else if (PRO == kProRmsInto) {
+        double ss = 0.0;
+        for (uint32_t k = ctid; k < K; k += NC) ss += static_cast<double>(p.x[k]) * static_cast<double>(p.x[k]);
+        ss = consumer_sum(ss, red);
+        const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
+        for (uint32_t blk = ctid; blk < nblk; blk += NC) {
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__fmul_rn(p.x[blk * 32 + e], scale), p.w_pre[blk * 32 + e]);
+            quant_block(v, blk, x16p, sx);
+        }
+    } else {
+        // Embed / Resid*: build the new residual in xs[K] first.
+        double ss = 0.0;
+        if (PRO == kProEmbed) {
+            uint32_t tok = *p.token;
+            if (tok >= p.vocab) {
+                if (ctid == 0 && blockIdx.x == 0) atomicOr(p.status, kStatusBadToken);
+                tok = 0;
+            }
+            for (uint32_t k = ctid; k < K; k += NC) {
+                const int8_t q = static_cast<int8_t>(p.embd[q8t_weight_offset(tok, k, K)]);
+                const uint64_t so = q8t_scale_offset(tok, k / 32, K);
+                const float sc = half_bits_to_float(p.embd[so] | (static_cast<uint32_t>(p.embd[so + 1]) << 8));
+                const float h = __fmul_rn(__fmul_rn(sc, static_cast<float>(q)), p.emb_scale);
+                xs[k] = h;
+                ss += static_cast<double>(h) * static_cast<double>(h);
+                if (blockIdx.x == 0) p.h_out[k] = h;
+            }
+            ss = consumer_sum(ss, red);
+        } else {
+            double so = 0.0;
+            for (uint32_t k = ctid; k < K; k += NC) so += static_cast<double>(p.x[k]) * static_cast<double>(p.x[k]);
+            so = consumer_sum(so, red);
+            const float post_scale = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(K)) + p.eps);
+            bool bad = false;
+            for (uint32_t k = ctid; k < K; k += NC) {
+                const float n = __fmul_rn(p.x[k], __fmul_rn(post_scale, p.w_post[k]));
+                const float h = __fadd_rn(n, p.h_prev[k]);
+                xs[k] = h;
+                bad |= !isfinite(h);
+                ss += static_cast<double>(h) * static_cast<double>(h);
+                if (blockIdx.x == 0) {
+                    if (PRO == kProResid) p.h_out[k] = h;
+                    if (p.trace) p.trace[k] = h;
+                }
+            }
+            if (bad && blockIdx.x == 0) atomicOr(p.status, kStatusNonFinite);
+            ss = consumer_sum(ss, red);
+        }
+        const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
+        named_bar_sync(1, NC);
+        for (uint32_t blk = ctid; blk < nblk; blk += NC) {
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const uint32_t k = blk * 32 + e;
+                // rms_norm_into: (x * scale) * w; rms_norm_inplace: x * (scale * w)
+                v[e] = (PRO == kProResidFinal) ? __fmul_rn(xs[k], __fmul_rn(scale, p.w_pre[k]))
+                                               : __fmul_rn(__fmul_rn(xs[k], scale), p.w_pre[k]);
+                if (PRO == kProResidFinal && blockIdx.x == 0) p.h_out[k] = v[e];
+            }
+            quant_block(v, blk, x16p, sx);
+        }
+    }
+    named_bar_sync(1, NC);
+
+    // ------------------------------------------------------- main loop
+    const uint32_t g_first = static_cast<uint32_t>(T0 / kt);
+    const uint32_t n_chunks = n_tiles ? (static_cast<uint32_t>((T1 - 1) / kt) - g_first) / kChunkGroups + 1 : 0;
+    const int quad = lane & 3;
+    int cur_g = -1;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    uint32_t chunks_done = 0;
+    unsigned long long best = 0ull;  // Argmax: lane 0 of each warp
+
+    auto flush = [&](int g) {
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        const uint32_t rel = static_cast<uint32_t>(g) - g_first;
+        float* part = partial + ((rel / kChunkGroups) & 1) * (kConsumerWarps * kChunkGroups * 16) +
+                      warp * (kChunkGroups * 16) + (rel % kChunkGroups) * 16 + 2 * (lane >> 2);
+        if (quad == 0) {
+            part[0] = acc0;
+            part[1] = acc1;
+        }
+        acc0 = 0.0f;
+        acc1 = 0.0f;
+    };
+
+    auto chunk_end = [&](uint32_t c) {
+        named_bar_sync(1, NC);
+        const uint32_t rel = c * kChunkGroups + warp;
+        const uint32_t g = g_first + rel;
+        const bool live = (static_cast<uint64_t>(g) * kt < T1) && ((static_cast<uint64_t>(g) + 1) * kt > T0);
+        if (!live) return;
+        float* part = partial + (c & 1) * (kConsumerWarps * kChunkGroups * 16) + warp * 16;
+        float v = 0.0f;
+        if (lane < 16) {
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                v += part[w * (kChunkGroups * 16) + lane];
+                part[w * (kChunkGroups * 16) + lane] = 0.0f;
+            }
+        }
+        const uint32_t row = g * kTileRows + lane;
+        if (EPI == kEpiAtomic) {
+            if (lane < 16 && row < p.rows) atomicAdd(p.y + row, v);
+        } else if (EPI == kEpiGeluPair) {
+            const float up = __shfl_down_sync(0xffffffffu, v, 8);
+            const uint32_t o = g * 8 + lane;
+            if (lane < 8 && o < p.rows / 2) p.y[o] = __fmul_rn(gelu_tanh(v), up);
+        } else {
+            unsigned long long key = 0ull;
+            if (lane < 16 && row < p.rows) {
+                if (p.y) p.y[row] = v;
+                if (!isnan(v)) key = argmax_key(v, p.row_base + row);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            best = key > best ? key : best;
+        }
+    };
+
+    for (uint32_t st = 0; st < n_stages; ++st) {
+        const uint32_t s = st % kStages;
+        if (!mbar_wait_bounded(&full[s], (st / kStages) & 1) && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
+        const uint64_t T = T0 + static_cast<uint64_t>(st) * kStageTiles + warp;
+        if (T < T1) {
+            const int g = static_cast<int>(T / kt);
+            const uint32_t j = static_cast<uint32_t>(T % kt);
+            if (g != cur_g && cur_g >= 0) flush(cur_g);
+            const uint32_t c = (static_cast<uint32_t>(g) - g_first) / kChunkGroups;
+            while (chunks_done < c) chunk_end(chunks_done++);
+            cur_g = g;
+            const uint8_t* tile = stages + s * kStageBytes + warp * kTileBytes;
+            const uint4* tq = reinterpret_cast<const uint4*>(tile);
+            const uint4 w0 = tq[lane], w1 = tq[32 + lane], w2 = tq[64 + lane], w3 = tq[96 + lane];
+            const uint32_t sc = reinterpret_cast<const uint32_t*>(tile + kTileQBytes)[lane];
+            const uint4* xp = reinterpret_cast<const uint4*>(x16p + j * 128);
+            const uint4 xa = xp[quad], xb = xp[4 + quad], xc = xp[8 + quad], xd = xp[12 + quad];
+            const int s0 = dot16(w1, xc, xd, dot16(w0, xa, xb, 0));
+            const int s1 = dot16(w3, xc, xd, dot16(w2, xa, xb, 0));
+            const float sxb = sx[j * 4 + quad];
+            acc0 += __fmul_rn(half_bits_to_float(sc & 0xffffu), sxb) * static_cast<float>(s0);
+            acc1 += __fmul_rn(half_bits_to_float(sc >> 16), sxb) * static_cast<float>(s1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (cur_g >= 0) flush(cur_g);
+    while (chunks_done < n_chunks) chunk_end(chunks_done++);
+
+    if (EPI == kEpiArgmax) {
+        unsigned long long* keys = reinterpret_cast<unsigned long long*>(red);
+        named_bar_sync(1, NC);
+        if (lane == 0) keys[warp] = best;
+        named_bar_sync(1, NC);
+        if (tid == 0) {
+            unsigned long long b = 0ull;
+            for (int w = 0; w < kConsumerWarps; ++w) b = keys[w] > b ? keys[w] : b;
+            if (b) atomicMax(p.amax, b);
+        }
+    }
+}
+
+}  // namespace vrt

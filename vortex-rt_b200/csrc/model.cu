@@ -1,0 +1,1426 @@
+// Gemma 3 Q8_0 model on one B200 (or one tensor-parallel rank): the device
+// arena, weight loading/repacking, the decode step as a chain of kernels
+// captured in a CUDA graph, and the C ABI of the model (the role of the
+// reference's Gemma3Model, src/gemma3.cpp).
+//
+// Arena (256-byte aligned pieces):
+//   token_embd       Q8T [vocab][d]          (embedding rows + tied LM head)
+//   per layer        Q8T qkv   [(Hl+2KVl)*hd][d]   q | k | v rows stacked
+//                    Q8T o     [d][Hl*hd]
+//                    Q8T gu    [2*ffl][d]          8 gate + 8 up rows per group
+//                    Q8T down  [d][ffl]
+//                    fp32 norms attn, q, k, post_attn, ffn, post_ffw
+//   output_norm      fp32 [d]
+// plus RoPE tables (host-computed cos/sin per position, as the reference's
+// build_rope_table), the KV cache (fp32, [KVl][cap][hd] per layer; cap =
+// window for sliding layers, positions for global ones) and activations.
+//
+// One decode step = per layer: QKV (embedding or residual + RMSNorm prologue)
+// -> attention -> o-proj -> gate/up (residual + 2 RMSNorm prologue, gelu*up
+// epilogue) -> down; then the LM head (residual + output norm prologue,
+// argmax epilogue) and a 1-thread finalize.  Each kernel clears, after its
+// griddepcontrol.wait, a buffer that a later kernel accumulates into and no
+// running kernel reads, so the graph needs no memset nodes and the PDL chain
+// is unbroken.  With tensor parallelism an NCCL all-reduce follows o-proj and
+// down, and an NCCL max-reduce merges the per-shard argmax keys.
+
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "vortexrt/gguf.hpp"
+#include "vrt_device.cuh"
+#include "vrt_internal.hpp"
+#include "vrt_kernels.hpp"
+
+namespace vrt {
+
+// ---------------------------------------------------------------- kernels
+
+struct RepackParams {
+    const uint8_t* src;      // raw Q8_0 rows
+    uint64_t src_row_bytes;
+    uint32_t src_blk0;       // first block of each source row to take
+    uint32_t rows;
+    uint32_t nblk;           // blocks per destination row
+    uint8_t* dst;            // Q8T matrix
+    uint32_t dst_cols;
+    uint32_t dst_row0;
+    int mode;                // 0: dst row = row0 + r; 1/2: gate/up interleave
+};
+
+__device__ __forceinline__ uint32_t dst_row_of(uint32_t r, uint32_t row0, int mode) {
+    if (mode == 0) return row0 + r;
+    return (r / 8) * 16 + (mode == 2 ? 8 : 0) + (r % 8);
+}
+
+__device__ __forceinline__ void store_q8t_block(uint8_t* dst, uint32_t cols, uint32_t row, uint32_t blk,
+                                                const uint8_t q[32], uint16_t scale_bits) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        w[i] = q[4 * i] | (static_cast<uint32_t>(q[4 * i + 1]) << 8) | (static_cast<uint32_t>(q[4 * i + 2]) << 16) |
+               (static_cast<uint32_t>(q[4 * i + 3]) << 24);
+    }
+    *reinterpret_cast<uint4*>(dst + q8t_weight_offset(row, blk * 32, cols)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(dst + q8t_weight_offset(row, blk * 32 + 16, cols)) = make_uint4(w[4], w[5], w[6], w[7]);
+    *reinterpret_cast<uint16_t*>(dst + q8t_scale_offset(row, blk, cols)) = scale_bits;
+}
+
+__global__ void repack_kernel(const RepackParams p) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<uint64_t>(p.rows) * p.nblk) return;
+    const uint32_t r = static_cast<uint32_t>(i / p.nblk), b = static_cast<uint32_t>(i % p.nblk);
+    const uint8_t* s = p.src + r * p.src_row_bytes + static_cast<uint64_t>(p.src_blk0 + b) * 34u;
+    uint8_t q[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) q[k] = s[2 + k];
+    store_q8t_block(p.dst, p.dst_cols, dst_row_of(r, p.dst_row0, p.mode), b, q,
+                    static_cast<uint16_t>(s[0] | (s[1] << 8)));
+}
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    uint64_t z = x;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ int32_t irwin_hall4(uint64_t key, uint64_t idx) {
+    const uint64_t h = splitmix64(key + idx);
+    const int64_t s = static_cast<int64_t>(h & 0xffff) + static_cast<int64_t>((h >> 16) & 0xffff) +
+                      static_cast<int64_t>((h >> 32) & 0xffff) + static_cast<int64_t>(h >> 48);
+    return static_cast<int32_t>(s - 131070);
+}
+
+struct SynthParams {
+    uint64_t key;
+    uint32_t cols_full;  // columns of the logical (unsharded) matrix
+    uint32_t r0, nr;     // source rows to generate
+    uint32_t b0, nb;     // source blocks per row to generate
+    float mult;
+    uint8_t* dst;
+    uint32_t dst_cols;
+    uint32_t dst_row0;
+    int mode;
+};
+
+// Same values and quantisation as synth_gguf.q8_matrix_bytes.
+__global__ void synth_q8_kernel(const SynthParams p) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<uint64_t>(p.nr) * p.nb) return;
+    const uint32_t r = static_cast<uint32_t>(i / p.nb), b = static_cast<uint32_t>(i % p.nb);
+    const uint64_t base = static_cast<uint64_t>(p.r0 + r) * p.cols_full + static_cast<uint64_t>(p.b0 + b) * 32u;
+    float v[32];
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        v[k] = __fmul_rn(static_cast<float>(irwin_hall4(p.key, base + k)), p.mult);
+        amax = fmaxf(amax, fabsf(v[k]));
+    }
+    const float scale = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+    const __half hs = __float2half_rn(scale);
+    const float dq = __half2float(hs);
+    uint8_t q[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        float t = rintf(__fdiv_rn(v[k], dq));
+        t = fminf(127.0f, fmaxf(-127.0f, t));
+        q[k] = static_cast<uint8_t>(static_cast<int8_t>(t));
+    }
+    store_q8t_block(p.dst, p.dst_cols, dst_row_of(r, p.dst_row0, p.mode), b, q, __half_as_ushort(hs));
+}
+
+__global__ void synth_norm_kernel(uint64_t key, uint32_t n, float mult, float* out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __fadd_rn(1.0f, __fmul_rn(static_cast<float>(irwin_hall4(key, i)), mult));
+}
+
+struct StepState {
+    uint32_t token;
+    uint32_t pos;
+    uint32_t status;
+    uint32_t out_count;
+    uint32_t prompt_count;
+    uint32_t result_index;
+    float result_value;
+    uint32_t pad;
+    unsigned long long key;
+};
+
+__global__ void finalize_decode_kernel(StepState* st, uint32_t vocab, uint32_t* out_ids, uint32_t out_cap) {
+    pdl_wait();
+    uint32_t idx;
+    float val;
+    argmax_unkey(st->key, &idx, &val);
+    st->result_index = idx;
+    st->result_value = val;
+    if (idx >= vocab || !isfinite(val)) st->status |= kStatusNonFinite;
+    const uint32_t c = st->out_count;
+    if (out_ids && c < out_cap) out_ids[c] = idx;
+    st->out_count = c + 1;
+    st->token = idx < vocab ? idx : 0u;
+    st->pos += 1;
+    st->key = 0ull;
+}
+
+__global__ void finalize_prefill_kernel(StepState* st, const uint32_t* prompt) {
+    pdl_wait();
+    const uint32_t p = st->pos + 1;
+    st->pos = p;
+    if (p < st->prompt_count) st->token = prompt[p];
+}
+
+// Final residual + output norm without the LM head (top_k == 0 steps).
+__global__ void final_hidden_kernel(const float* dn, const float* h_prev, const float* w_post, const float* w_out,
+                                    float* hidden, float* trace, uint32_t d, float eps, uint32_t* status) {
+    pdl_wait();
+    __shared__ double red[32];
+    __shared__ float scale_s;
+    extern __shared__ float hs[];
+    const int tid = threadIdx.x;
+    double so = 0.0;
+    for (uint32_t k = tid; k < d; k += blockDim.x) so += static_cast<double>(dn[k]) * static_cast<double>(dn[k]);
+    so = warp_sum(so);
+    if ((tid & 31) == 0) red[tid / 32] = so;
+    __syncthreads();
+    if (tid == 0) {
+        double s = 0.0;
+        for (uint32_t w = 0; w < blockDim.x / 32; ++w) s += red[w];
+        scale_s = 1.0f / sqrtf(static_cast<float>(s / static_cast<double>(d)) + eps);
+    }
+    __syncthreads();
+    const float ps = scale_s;
+    double ss = 0.0;
+    bool bad = false;
+    for (uint32_t k = tid; k < d; k += blockDim.x) {
+        const float h = __fadd_rn(__fmul_rn(dn[k], __fmul_rn(ps, w_post[k])), h_prev[k]);
+        hs[k] = h;
+        bad |= !isfinite(h);
+        if (trace) trace[k] = h;
+        ss += static_cast<double>(h) * static_cast<double>(h);
+    }
+    if (bad) atomicOr(status, kStatusNonFinite);
+    __syncthreads();
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid / 32] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double s = 0.0;
+        for (uint32_t w = 0; w < blockDim.x / 32; ++w) s += red[w];
+        scale_s = 1.0f / sqrtf(static_cast<float>(s / static_cast<double>(d)) + eps);
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    for (uint32_t k = tid; k < d; k += blockDim.x) hidden[k] = __fmul_rn(hs[k], __fmul_rn(sc, w_out[k]));
+}
+
+// ------------------------------------------------------------------ host
+
+constexpr uint32_t kMaxSteps = 1u << 16;  // capacity of the generated-id ring
+
+struct LayerW {
+    uint64_t qkv, o, gu, down;
+    uint64_t n_attn, n_q, n_k, n_post_attn, n_ffn, n_post_ffw;
+    float* k_cache;
+    float* v_cache;
+    uint32_t cap;
+    bool global;
+    uint32_t splits;
+};
+
+// minimal NCCL surface, resolved at run time so single-GPU use needs no NCCL
+struct Nccl {
+    void* lib = nullptr;
+    int (*CommInitRank)(void**, int, const void*, int) = nullptr;  // ncclUniqueId passed by value -> by pointer shim
+    int (*AllReduce)(const void*, void*, size_t, int, int, void*, cudaStream_t) = nullptr;
+    int (*CommDestroy)(void*) = nullptr;
+    int (*GetUniqueId)(void*) = nullptr;
+    const char* (*GetErrorString)(int) = nullptr;
+};
+
+}  // namespace vrt
+
+struct vrt_model {
+    vrt_ctx* ctx = nullptr;
+    vrt_gemma3_config cfg{};
+    vrt_model_options opt{};
+    uint64_t eos = 1;
+    int rank = 0, world = 1;
+    uint32_t Hl = 0, KVl = 0, qwl = 0, kwl = 0, ffl = 0, vocab_lo = 0, vocab_hi = 0;
+    uint8_t* arena = nullptr;
+    uint64_t arena_bytes = 0;
+    uint64_t embd = 0, out_norm = 0;
+    std::vector<vrt::LayerW> layers;
+    uint32_t P = 0;  // positions (rope/KV capacity)
+    float *rope_cos_l = nullptr, *rope_sin_l = nullptr, *rope_cos_g = nullptr, *rope_sin_g = nullptr;
+    float* kv_mem = nullptr;
+    float* act_mem = nullptr;
+    float *h0, *h1, *qkv, *att, *o, *act, *dn, *hidden, *logits, *trace, *part_ml, *part_acc;
+    uint32_t* tickets = nullptr;
+    uint32_t* out_ids = nullptr;
+    uint32_t* prompt = nullptr;
+    vrt::StepState* st = nullptr;      // device
+    vrt::StepState* st_host = nullptr; // pinned mirror
+    float* hidden_host = nullptr;      // pinned
+    uint32_t next_pos = 0;
+    uint32_t generated = 0;  // ids in out_ids since the last prefill
+    bool trace_on = false;
+    cudaGraphExec_t g_head = nullptr, g_nohead = nullptr;
+    uint32_t kernels_per_step = 0;
+    void* comm = nullptr;
+    unsigned long long* key_tmp = nullptr;
+    vrt::Nccl nccl;
+};
+
+namespace vrt {
+
+static int nccl_load(Nccl& n) {
+    if (n.lib) return VRT_OK;
+    const char* names[] = {"libnccl.so.2", "libnccl.so"};
+    for (const char* nm : names) {
+        n.lib = dlopen(nm, RTLD_NOW | RTLD_GLOBAL);
+        if (n.lib) break;
+    }
+    if (!n.lib) return fail(VRT_E_UNSUPPORTED, "tensor parallelism needs libnccl.so.2: %s", dlerror());
+    n.AllReduce = reinterpret_cast<decltype(n.AllReduce)>(dlsym(n.lib, "ncclAllReduce"));
+    n.CommDestroy = reinterpret_cast<decltype(n.CommDestroy)>(dlsym(n.lib, "ncclCommDestroy"));
+    n.GetUniqueId = reinterpret_cast<decltype(n.GetUniqueId)>(dlsym(n.lib, "ncclGetUniqueId"));
+    n.GetErrorString = reinterpret_cast<decltype(n.GetErrorString)>(dlsym(n.lib, "ncclGetErrorString"));
+    if (!n.AllReduce || !n.CommDestroy || !n.GetUniqueId || !n.GetErrorString) {
+        return fail(VRT_E_UNSUPPORTED, "libnccl.so.2 lacks the expected symbols");
+    }
+    return VRT_OK;
+}
+
+// ncclCommInitRank takes ncclUniqueId (128 bytes) by value.
+struct NcclId {
+    char b[128];
+};
+using CommInitRankFn = int (*)(void**, int, NcclId, int);
+
+static uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
+
+static uint64_t fnv1a64(const std::string& s) {
+    uint64_t h = 0xCBF29CE484222325ull;
+    for (unsigned char c : s) {
+        h ^= c;
+        h *= 0x100000001B3ull;
+    }
+    return h;
+}
+static uint64_t splitmix64_h(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    uint64_t z = x;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static uint64_t stream_key(uint64_t seed, const std::string& name) {
+    return splitmix64_h(seed ^ ((fnv1a64(name) + 1ull) * 0xD1B54A32D192ED03ull));
+}
+
+static std::string lname(uint32_t l, const char* suffix) { return "blk." + std::to_string(l) + "." + suffix; }
+
+static int validate_config(const vrt_gemma3_config& c) {
+    if (!c.embedding_length || !c.block_count || !c.feed_forward_length || !c.head_count || !c.head_count_kv ||
+        !c.head_dim || !c.value_dim || !c.vocab_size) {
+        return fail(VRT_E_INVALID, "Gemma 3 configuration contains zero dimensions");
+    }
+    if (c.head_count % c.head_count_kv) return fail(VRT_E_INVALID, "Gemma 3 head_count must be divisible by head_count_kv");
+    if (c.value_dim != c.head_dim) return fail(VRT_E_UNSUPPORTED, "key and value head dimensions must be equal");
+    if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) {
+        return fail(VRT_E_UNSUPPORTED, "head_dim %u unsupported (64, 128 or 256)", c.head_dim);
+    }
+    if (c.head_count / c.head_count_kv > 8) return fail(VRT_E_UNSUPPORTED, "more than 8 query heads per KV head");
+    if (c.embedding_length % 128 || c.feed_forward_length % 128 || (c.head_count * c.head_dim) % 128) {
+        return fail(VRT_E_UNSUPPORTED, "model widths must be multiples of 128");
+    }
+    return VRT_OK;
+}
+
+// Shard sizes and the arena plan.
+static int plan(vrt_model* m) {
+    const auto& c = m->cfg;
+    const int W = m->world;
+    if (c.head_count_kv % W || c.head_count % W || c.feed_forward_length % (W * 128) || c.vocab_size % (W * 16)) {
+        return fail(VRT_E_UNSUPPORTED, "model does not split evenly over %d ranks", W);
+    }
+    m->Hl = c.head_count / W;
+    m->KVl = c.head_count_kv / W;
+    m->qwl = m->Hl * c.head_dim;
+    m->kwl = m->KVl * c.head_dim;
+    m->ffl = c.feed_forward_length / W;
+    if (m->qwl % 128) return fail(VRT_E_UNSUPPORTED, "per-rank attention width must be a multiple of 128");
+    m->vocab_lo = c.vocab_size / W * m->rank;
+    m->vocab_hi = c.vocab_size / W * (m->rank + 1);
+    const uint32_t d = c.embedding_length;
+    uint64_t at = 0;
+    m->embd = at;
+    at = align256(at + q8t_bytes(c.vocab_size, d));
+    m->layers.resize(c.block_count);
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        auto& L = m->layers[l];
+        L.qkv = at;
+        at = align256(at + q8t_bytes(m->qwl + 2 * m->kwl, d));
+        L.o = at;
+        at = align256(at + q8t_bytes(d, m->qwl));
+        L.gu = at;
+        at = align256(at + q8t_bytes(2 * m->ffl, d));
+        L.down = at;
+        at = align256(at + q8t_bytes(d, m->ffl));
+        L.n_attn = at;
+        at = align256(at + 4ull * d);
+        L.n_q = at;
+        at = align256(at + 4ull * c.head_dim);
+        L.n_k = at;
+        at = align256(at + 4ull * c.head_dim);
+        L.n_post_attn = at;
+        at = align256(at + 4ull * d);
+        L.n_ffn = at;
+        at = align256(at + 4ull * d);
+        L.n_post_ffw = at;
+        at = align256(at + 4ull * d);
+        L.global = ((l + 1u) % 6u) == 0u;  // gemma3.cpp:1301-1307
+    }
+    m->out_norm = at;
+    at = align256(at + 4ull * d);
+    m->arena_bytes = at + 4096;
+    return VRT_OK;
+}
+
+static void host_rope_table(uint32_t hd, float theta, uint32_t P, std::vector<float>& cs, std::vector<float>& sn) {
+    // build_rope_inverse_frequencies + build_rope_table (src/gemma3.cpp:1309-1369)
+    const uint32_t half = hd / 2;
+    std::vector<float> inv(half);
+    for (uint32_t i = 0; i < half; ++i) {
+        const float e = (2.0f * static_cast<float>(i)) / static_cast<float>(hd);
+        inv[i] = 1.0f / std::pow(theta, e);
+    }
+    cs.resize(static_cast<size_t>(P) * half);
+    sn.resize(static_cast<size_t>(P) * half);
+    for (uint32_t p = 0; p < P; ++p) {
+        const float pf = static_cast<float>(p);
+        for (uint32_t i = 0; i < half; ++i) {
+            const float a = pf * inv[i];
+            cs[static_cast<size_t>(p) * half + i] = std::cos(a);
+            sn[static_cast<size_t>(p) * half + i] = std::sin(a);
+        }
+    }
+}
+
+static int alloc_runtime(vrt_model* m) {
+    const auto& c = m->cfg;
+    vrt_ctx* ctx = m->ctx;
+    const uint32_t d = c.embedding_length, hd = c.head_dim;
+    uint32_t P = m->opt.max_positions ? m->opt.max_positions : std::min<uint32_t>(c.context_length, 8192u);
+    if (c.context_length && P > c.context_length) P = c.context_length;
+    if (P == 0) return fail(VRT_E_INVALID, "no positions available");
+    m->P = P;
+    VRT_CUDA(cudaMalloc(&m->arena, m->arena_bytes));
+    VRT_CUDA(cudaMemsetAsync(m->arena, 0, m->arena_bytes, ctx->stream));
+    // KV cache
+    uint64_t kv_floats = 0;
+    const int sms = ctx->prop.multiProcessorCount;
+    uint32_t max_splits = 1;
+    for (auto& L : m->layers) {
+        L.cap = (!L.global && c.sliding_window) ? std::min(c.sliding_window, P) : P;
+        kv_floats += 2ull * m->KVl * L.cap * hd;
+        const uint32_t by_len = std::max(1u, (L.cap + 15) / 16);
+        const uint32_t by_sm = std::max(1u, static_cast<uint32_t>(2 * sms) / m->KVl);
+        L.splits = std::min(by_len, by_sm);
+        max_splits = std::max(max_splits, L.splits);
+    }
+    VRT_CUDA(cudaMalloc(&m->kv_mem, kv_floats * 4));
+    VRT_CUDA(cudaMemsetAsync(m->kv_mem, 0, kv_floats * 4, ctx->stream));
+    float* kp = m->kv_mem;
+    for (auto& L : m->layers) {
+        L.k_cache = kp;
+        kp += static_cast<uint64_t>(m->KVl) * L.cap * hd;
+        L.v_cache = kp;
+        kp += static_cast<uint64_t>(m->KVl) * L.cap * hd;
+    }
+    // RoPE tables
+    std::vector<float> cs, sn;
+    const uint64_t tab = static_cast<uint64_t>(P) * (hd / 2) * 4;
+    float* rope = nullptr;
+    VRT_CUDA(cudaMalloc(&rope, 4 * tab));
+    m->rope_cos_l = rope;
+    m->rope_sin_l = rope + tab / 4;
+    m->rope_cos_g = rope + 2 * (tab / 4);
+    m->rope_sin_g = rope + 3 * (tab / 4);
+    host_rope_table(hd, c.local_rope_base, P, cs, sn);
+    VRT_CUDA(cudaMemcpy(m->rope_cos_l, cs.data(), tab, cudaMemcpyHostToDevice));
+    VRT_CUDA(cudaMemcpy(m->rope_sin_l, sn.data(), tab, cudaMemcpyHostToDevice));
+    host_rope_table(hd, c.global_rope_base, P, cs, sn);
+    VRT_CUDA(cudaMemcpy(m->rope_cos_g, cs.data(), tab, cudaMemcpyHostToDevice));
+    VRT_CUDA(cudaMemcpy(m->rope_sin_g, sn.data(), tab, cudaMemcpyHostToDevice));
+    // activations
+    const uint32_t vl = m->vocab_hi - m->vocab_lo;
+    const uint64_t sizes[] = {d, d, m->qwl + 2ull * m->kwl, m->qwl, d, m->ffl, d, d, vl,
+                              static_cast<uint64_t>(c.block_count) * d,
+                              static_cast<uint64_t>(m->Hl) * max_splits * 2,
+                              static_cast<uint64_t>(m->Hl) * max_splits * hd};
+    uint64_t total = 0;
+    for (auto s : sizes) total += align256(s * 4) / 4;
+    VRT_CUDA(cudaMalloc(&m->act_mem, total * 4));
+    VRT_CUDA(cudaMemsetAsync(m->act_mem, 0, total * 4, ctx->stream));
+    float* ap = m->act_mem;
+    float** dst[] = {&m->h0, &m->h1, &m->qkv, &m->att, &m->o, &m->act, &m->dn, &m->hidden, &m->logits, &m->trace,
+                     &m->part_ml, &m->part_acc};
+    for (size_t i = 0; i < 12; ++i) {
+        *dst[i] = ap;
+        ap += align256(sizes[i] * 4) / 4;
+    }
+    VRT_CUDA(cudaMalloc(&m->tickets, 4ull * std::max(1u, m->KVl)));
+    VRT_CUDA(cudaMemsetAsync(m->tickets, 0, 4ull * std::max(1u, m->KVl), ctx->stream));
+    VRT_CUDA(cudaMalloc(&m->out_ids, 4ull * kMaxSteps));
+    VRT_CUDA(cudaMalloc(&m->prompt, 4ull * P));
+    VRT_CUDA(cudaMalloc(&m->st, sizeof(StepState)));
+    VRT_CUDA(cudaMemsetAsync(m->st, 0, sizeof(StepState), ctx->stream));
+    VRT_CUDA(cudaMalloc(&m->key_tmp, 8));
+    VRT_CUDA(cudaMallocHost(&m->st_host, sizeof(StepState)));
+    VRT_CUDA(cudaMallocHost(&m->hidden_host, 4ull * d));
+    VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+    return VRT_OK;
+}
+
+// ------------------------------------------------------- weight loading
+
+struct Loader {
+    vrt_model* m;
+    uint8_t* h_stage = nullptr;  // pinned
+    uint8_t* d_stage = nullptr;
+    uint64_t cap = 64ull << 20;
+    ~Loader() {
+        if (h_stage) cudaFreeHost(h_stage);
+        if (d_stage) cudaFree(d_stage);
+    }
+    int init() {
+        VRT_CUDA(cudaMallocHost(&h_stage, cap));
+        VRT_CUDA(cudaMalloc(&d_stage, cap));
+        return VRT_OK;
+    }
+    // rows [r0, r0+nr) x blocks [b0, b0+nb) of a raw Q8_0 tensor -> Q8T destination
+    int q8(const uint8_t* src, uint32_t src_cols, uint32_t r0, uint32_t nr, uint32_t b0, uint32_t nb, uint8_t* dst,
+           uint32_t dst_cols, uint32_t dst_row0, int mode) {
+        const uint64_t src_row_bytes = static_cast<uint64_t>(src_cols) / 32 * 34;
+        const uint64_t take = static_cast<uint64_t>(nb) * 34;
+        // chunks of whole 8-row groups keep the gate/up interleave aligned
+        const uint32_t rows_per = static_cast<uint32_t>(std::max<uint64_t>(8, cap / take / 8 * 8));
+        cudaStream_t s = m->ctx->stream;
+        for (uint32_t r = 0; r < nr; r += rows_per) {
+            const uint32_t n = std::min(rows_per, nr - r);
+            for (uint32_t i = 0; i < n; ++i) {
+                memcpy(h_stage + i * take, src + (static_cast<uint64_t>(r0 + r + i)) * src_row_bytes + b0 * 34ull, take);
+            }
+            VRT_CUDA(cudaMemcpyAsync(d_stage, h_stage, n * take, cudaMemcpyHostToDevice, s));
+            RepackParams p{d_stage, take, 0, n, nb, dst, dst_cols, 0, mode};
+            if (mode == 0) {
+                p.dst_row0 = dst_row0 + r;
+            } else {
+                // interleave keeps source-row numbering: offset the destination by whole groups
+                p.dst = dst + static_cast<uint64_t>(r / 8) * (dst_cols / kTileCols) * kTileBytes;
+                if (r % 8) return fail(VRT_E_INVALID, "interleaved repack chunk not group aligned");
+            }
+            const uint64_t work = static_cast<uint64_t>(n) * nb;
+            VRT_CUDA(launch(repack_kernel, dim3(static_cast<unsigned>((work + 255) / 256)), dim3(256), 0, s, false, p));
+            VRT_CUDA(cudaStreamSynchronize(s));
+        }
+        return VRT_OK;
+    }
+};
+
+static int read_config(const vortexrt::GgufFile& g, vrt_gemma3_config& c, uint64_t& eos) {
+    // Gemma3Model::Gemma3Model config section (src/gemma3.cpp:174-257)
+    if (g.metadata_string("general.architecture") != std::optional<std::string>{"gemma3"}) {
+        return fail(VRT_E_INVALID, "Gemma3Model requires general.architecture=gemma3");
+    }
+    auto u32 = [&](const char* key, uint32_t& out) -> int {
+        const auto v = g.metadata_u64(key);
+        if (!v || *v > 0xffffffffull) return fail(VRT_E_INVALID, "Missing/invalid Gemma 3 metadata: %s", key);
+        out = static_cast<uint32_t>(*v);
+        return VRT_OK;
+    };
+    VRT_TRY(u32("gemma3.context_length", c.context_length));
+    VRT_TRY(u32("gemma3.embedding_length", c.embedding_length));
+    VRT_TRY(u32("gemma3.block_count", c.block_count));
+    VRT_TRY(u32("gemma3.feed_forward_length", c.feed_forward_length));
+    VRT_TRY(u32("gemma3.attention.head_count", c.head_count));
+    VRT_TRY(u32("gemma3.attention.head_count_kv", c.head_count_kv));
+    VRT_TRY(u32("gemma3.attention.key_length", c.head_dim));
+    VRT_TRY(u32("gemma3.attention.value_length", c.value_dim));
+    const auto* eps = g.find_metadata("gemma3.attention.layer_norm_rms_epsilon");
+    if (!eps) return fail(VRT_E_INVALID, "Missing Gemma 3 metadata: gemma3.attention.layer_norm_rms_epsilon");
+    const auto ev = eps->as_f64();
+    if (!ev || !std::isfinite(*ev)) return fail(VRT_E_INVALID, "Invalid Gemma 3 floating metadata: gemma3.attention.layer_norm_rms_epsilon");
+    c.rms_epsilon = static_cast<float>(*ev);
+    c.sliding_window = 0;
+    if (const auto sw = g.metadata_u64("gemma3.attention.sliding_window"); sw && *sw <= 0xffffffffull) {
+        c.sliding_window = static_cast<uint32_t>(*sw);
+    }
+    c.global_rope_base = 1.0e6f;
+    c.local_rope_base = 1.0e4f;
+    if (const auto* r = g.find_metadata("gemma3.rope.freq_base")) {
+        if (const auto v = r->as_f64(); v && std::isfinite(*v) && *v > 0.0) c.global_rope_base = static_cast<float>(*v);
+    }
+    const auto* emb = g.find_tensor("token_embd.weight");
+    if (!emb) return fail(VRT_E_INVALID, "Missing Gemma 3 tensor: token_embd.weight");
+    if (emb->type != 8 || emb->dimensions.size() != 2 || emb->dimensions[0] != c.embedding_length ||
+        emb->dimensions[1] > 0xffffffffull) {
+        return fail(VRT_E_INVALID, "Unsupported token_embd.weight layout");
+    }
+    c.vocab_size = static_cast<uint32_t>(emb->dimensions[1]);
+    eos = g.metadata_u64("tokenizer.ggml.eos_token_id").value_or(1);
+    return validate_config(c);
+}
+
+static int load_weights(vrt_model* m, const vortexrt::GgufFile& g) {
+    const auto& c = m->cfg;
+    const uint32_t d = c.embedding_length, hd = c.head_dim;
+    Loader ld{m};
+    VRT_TRY(ld.init());
+    auto q8 = [&](const std::string& name, uint64_t cols, uint64_t rows) -> const uint8_t* {
+        const auto* t = g.find_tensor(name);
+        if (!t || t->type != 8 || t->dimensions.size() != 2 || t->dimensions[0] != cols || t->dimensions[1] != rows) {
+            return nullptr;
+        }
+        return g.tensor_data(*t);
+    };
+    auto f32 = [&](const std::string& name, uint64_t n, uint64_t dst) -> int {
+        const auto* t = g.find_tensor(name);
+        if (!t || t->type != 0 || t->dimensions.size() != 1 || t->dimensions[0] != n) {
+            return fail(VRT_E_INVALID, "Missing or mis-shaped Gemma 3 tensor: %s", name.c_str());
+        }
+        VRT_CUDA(cudaMemcpy(m->arena + dst, g.tensor_data(*t), n * 4, cudaMemcpyHostToDevice));
+        return VRT_OK;
+    };
+    const uint8_t* emb = q8("token_embd.weight", d, c.vocab_size);
+    if (!emb) return fail(VRT_E_INVALID, "Unsupported token_embd.weight layout");
+    VRT_TRY(ld.q8(emb, d, 0, c.vocab_size, 0, d / 32, m->arena + m->embd, d, 0, 0));
+    const uint32_t h0 = m->Hl * m->rank, g0 = m->KVl * m->rank, f0 = m->ffl * m->rank;
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const auto& L = m->layers[l];
+        const uint8_t* wq = q8(lname(l, "attn_q.weight"), d, static_cast<uint64_t>(c.head_count) * hd);
+        const uint8_t* wk = q8(lname(l, "attn_k.weight"), d, static_cast<uint64_t>(c.head_count_kv) * hd);
+        const uint8_t* wv = q8(lname(l, "attn_v.weight"), d, static_cast<uint64_t>(c.head_count_kv) * hd);
+        const uint8_t* wo = q8(lname(l, "attn_output.weight"), static_cast<uint64_t>(c.head_count) * hd, d);
+        const uint8_t* wg = q8(lname(l, "ffn_gate.weight"), d, c.feed_forward_length);
+        const uint8_t* wu = q8(lname(l, "ffn_up.weight"), d, c.feed_forward_length);
+        const uint8_t* wd = q8(lname(l, "ffn_down.weight"), c.feed_forward_length, d);
+        if (!wq || !wk || !wv || !wo || !wg || !wu || !wd) {
+            return fail(VRT_E_INVALID, "Missing or mis-shaped Q8_0 projection in layer %u", l);
+        }
+        uint8_t* qkv = m->arena + L.qkv;
+        VRT_TRY(ld.q8(wq, d, h0 * hd, m->qwl, 0, d / 32, qkv, d, 0, 0));
+        VRT_TRY(ld.q8(wk, d, g0 * hd, m->kwl, 0, d / 32, qkv, d, m->qwl, 0));
+        VRT_TRY(ld.q8(wv, d, g0 * hd, m->kwl, 0, d / 32, qkv, d, m->qwl + m->kwl, 0));
+        VRT_TRY(ld.q8(wo, c.head_count * hd, 0, d, h0 * hd / 32, m->qwl / 32, m->arena + L.o, m->qwl, 0, 0));
+        VRT_TRY(ld.q8(wg, d, f0, m->ffl, 0, d / 32, m->arena + L.gu, d, 0, 1));
+        VRT_TRY(ld.q8(wu, d, f0, m->ffl, 0, d / 32, m->arena + L.gu, d, 0, 2));
+        VRT_TRY(ld.q8(wd, c.feed_forward_length, 0, d, f0 / 32, m->ffl / 32, m->arena + L.down, m->ffl, 0, 0));
+        VRT_TRY(f32(lname(l, "attn_norm.weight"), d, L.n_attn));
+        VRT_TRY(f32(lname(l, "attn_q_norm.weight"), hd, L.n_q));
+        VRT_TRY(f32(lname(l, "attn_k_norm.weight"), hd, L.n_k));
+        VRT_TRY(f32(lname(l, "post_attention_norm.weight"), d, L.n_post_attn));
+        VRT_TRY(f32(lname(l, "ffn_norm.weight"), d, L.n_ffn));
+        VRT_TRY(f32(lname(l, "post_ffw_norm.weight"), d, L.n_post_ffw));
+    }
+    VRT_TRY(f32("output_norm.weight", d, m->out_norm));
+    return VRT_OK;
+}
+
+static int synth_weights(vrt_model* m, uint64_t seed) {
+    const auto& c = m->cfg;
+    const uint32_t d = c.embedding_length, hd = c.head_dim;
+    cudaStream_t s = m->ctx->stream;
+    const float mult_w = static_cast<float>(0.02 / 37837.2265);
+    const float mult_n = static_cast<float>(0.1 / 37837.2265);
+    auto gen = [&](const std::string& name, uint32_t cols_full, uint32_t r0, uint32_t nr, uint32_t b0, uint32_t nb,
+                   uint64_t dst, uint32_t dst_cols, uint32_t dst_row0, int mode) -> int {
+        SynthParams p{stream_key(seed, name), cols_full, r0, nr, b0, nb, mult_w, m->arena + dst, dst_cols, dst_row0, mode};
+        const uint64_t work = static_cast<uint64_t>(nr) * nb;
+        VRT_CUDA(launch(synth_q8_kernel, dim3(static_cast<unsigned>((work + 255) / 256)), dim3(256), 0, s, false, p));
+        return VRT_OK;
+    };
+    auto norm = [&](const std::string& name, uint32_t n, uint64_t dst) -> int {
+        VRT_CUDA(launch(synth_norm_kernel, dim3((n + 255) / 256), dim3(256), 0, s, false, stream_key(seed, name), n,
+                        mult_n, reinterpret_cast<float*>(m->arena + dst)));
+        return VRT_OK;
+    };
+    VRT_TRY(gen("token_embd.weight", d, 0, c.vocab_size, 0, d / 32, m->embd, d, 0, 0));
+    const uint32_t h0 = m->Hl * m->rank, g0 = m->KVl * m->rank, f0 = m->ffl * m->rank;
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const auto& L = m->layers[l];
+        VRT_TRY(gen(lname(l, "attn_q.weight"), d, h0 * hd, m->qwl, 0, d / 32, L.qkv, d, 0, 0));
+        VRT_TRY(gen(lname(l, "attn_k.weight"), d, g0 * hd, m->kwl, 0, d / 32, L.qkv, d, m->qwl, 0));
+        VRT_TRY(gen(lname(l, "attn_v.weight"), d, g0 * hd, m->kwl, 0, d / 32, L.qkv, d, m->qwl + m->kwl, 0));
+        VRT_TRY(gen(lname(l, "attn_output.weight"), c.head_count * hd, 0, d, h0 * hd / 32, m->qwl / 32, L.o, m->qwl, 0, 0));
+        VRT_TRY(gen(lname(l, "ffn_gate.weight"), d, f0, m->ffl, 0, d / 32, L.gu, d, 0, 1));
+        VRT_TRY(gen(lname(l, "ffn_up.weight"), d, f0, m->ffl, 0, d / 32, L.gu, d, 0, 2));
+        VRT_TRY(gen(lname(l, "ffn_down.weight"), c.feed_forward_length, 0, d, f0 / 32, m->ffl / 32, L.down, m->ffl, 0, 0));
+        VRT_TRY(norm(lname(l, "attn_norm.weight"), d, L.n_attn));
+        VRT_TRY(norm(lname(l, "attn_q_norm.weight"), hd, L.n_q));
+        VRT_TRY(norm(lname(l, "attn_k_norm.weight"), hd, L.n_k));
+        VRT_TRY(norm(lname(l, "post_attention_norm.weight"), d, L.n_post_attn));
+        VRT_TRY(norm(lname(l, "ffn_norm.weight"), d, L.n_ffn));
+        VRT_TRY(norm(lname(l, "post_ffw_norm.weight"), d, L.n_post_ffw));
+    }
+    VRT_TRY(norm("output_norm.weight", d, m->out_norm));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    return VRT_OK;
+}
+
+// ------------------------------------------------------------ the step
+
+static int nccl_sum(vrt_model* m, float* buf, size_t n, cudaStream_t s) {
+    if (m->world <= 1) return VRT_OK;
+    const int r = m->nccl.AllReduce(buf, buf, n, /*ncclFloat32*/ 7, /*ncclSum*/ 0, m->comm, s);
+    if (r) return fail(VRT_E_CUDA, "ncclAllReduce failed: %s", m->nccl.GetErrorString(r));
+    return VRT_OK;
+}
+
+static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernels) {
+    const auto& c = m->cfg;
+    const bool pdl = m->opt.use_pdl != 0;
+    const int sms = m->ctx->prop.multiProcessorCount;
+    const uint32_t d = c.embedding_length, hd = c.head_dim;
+    uint32_t nk = 0;
+    uint32_t* status = &m->st->status;
+    float* trace = m->trace_on ? m->trace : nullptr;
+    auto F = [&](uint64_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+    auto gemv = [&](int pro, int epi, GemvParams p) -> int {
+        p.status = status;
+        p.eps = c.rms_epsilon;
+        VRT_CUDA(gemv_q8t(pro, epi, p, gemv_grid(sms, p.rows), s, pdl));
+        ++nk;
+        return VRT_OK;
+    };
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const auto& L = m->layers[l];
+        // QKV
+        {
+            GemvParams p{};
+            p.w = m->arena + L.qkv;
+            p.rows = m->qwl + 2 * m->kwl;
+            p.cols = d;
+            p.w_pre = F(L.n_attn);
+            p.h_out = m->h0;
+            p.y = m->qkv;
+            if (l == 0) {
+                p.embd = m->arena + m->embd;
+                p.token = &m->st->token;
+                p.vocab = c.vocab_size;
+                p.emb_scale = std::sqrt(static_cast<float>(d));
+                VRT_TRY(gemv(kProEmbed, kEpiAtomic, p));
+            } else {
+                p.x = m->dn;
+                p.h_prev = m->h1;
+                p.w_post = F(m->layers[l - 1].n_post_ffw);
+                p.trace = trace ? trace + static_cast<uint64_t>(l - 1) * d : nullptr;
+                VRT_TRY(gemv(kProResid, kEpiAtomic, p));
+            }
+        }
+        // attention (clears dn for this layer's down projection)
+        {
+            AttnParams a{};
+            a.qkv = m->qkv;
+            a.q_norm = F(L.n_q);
+            a.k_norm = F(L.n_k);
+            a.rope_cos = L.global ? m->rope_cos_g : m->rope_cos_l;
+            a.rope_sin = L.global ? m->rope_sin_g : m->rope_sin_l;
+            a.k_cache = L.k_cache;
+            a.v_cache = L.v_cache;
+            a.cap = L.cap;
+            a.window = L.global ? 0u : c.sliding_window;
+            a.pos = &m->st->pos;
+            a.H = m->Hl;
+            a.KV = m->KVl;
+            a.hd = hd;
+            a.eps = c.rms_epsilon;
+            a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+            a.part_ml = m->part_ml;
+            a.part_acc = m->part_acc;
+            a.tickets = m->tickets;
+            a.out = m->att;
+            a.splits = L.splits;
+            a.zero0 = m->dn;
+            a.zero0_count = d;
+            VRT_CUDA(attention_launch(a, dim3(L.splits, m->KVl), s, pdl));
+            ++nk;
+        }
+        // o-proj (clears qkv for the next QKV)
+        {
+            GemvParams p{};
+            p.w = m->arena + L.o;
+            p.rows = d;
+            p.cols = m->qwl;
+            p.x = m->att;
+            p.y = m->o;
+            p.zero0 = m->qkv;
+            p.zero0_count = m->qwl + 2 * m->kwl;
+            VRT_TRY(gemv(kProPlain, kEpiAtomic, p));
+            VRT_TRY(nccl_sum(m, m->o, d, s));
+        }
+        // gate/up with residual + post-attention norm + ffn norm
+        {
+            GemvParams p{};
+            p.w = m->arena + L.gu;
+            p.rows = 2 * m->ffl;
+            p.cols = d;
+            p.x = m->o;
+            p.h_prev = m->h0;
+            p.w_post = F(L.n_post_attn);
+            p.w_pre = F(L.n_ffn);
+            p.h_out = m->h1;
+            p.y = m->act;
+            VRT_TRY(gemv(kProResid, kEpiGeluPair, p));
+        }
+        // down (clears o for the next o-proj)
+        {
+            GemvParams p{};
+            p.w = m->arena + L.down;
+            p.rows = d;
+            p.cols = m->ffl;
+            p.x = m->act;
+            p.y = m->dn;
+            p.zero0 = m->o;
+            p.zero0_count = d;
+            VRT_TRY(gemv(kProPlain, kEpiAtomic, p));
+            VRT_TRY(nccl_sum(m, m->dn, d, s));
+        }
+    }
+    const auto& last = m->layers[c.block_count - 1];
+    float* tlast = trace ? trace + static_cast<uint64_t>(c.block_count - 1) * d : nullptr;
+    if (head) {
+        GemvParams p{};
+        const uint32_t kt = d / kTileCols;
+        p.w = m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes;
+        p.rows = m->vocab_hi - m->vocab_lo;
+        p.cols = d;
+        p.x = m->dn;
+        p.h_prev = m->h1;
+        p.w_post = F(last.n_post_ffw);
+        p.w_pre = F(m->out_norm);
+        p.h_out = m->hidden;
+        p.trace = tlast;
+        p.y = m->logits;
+        p.amax = &m->st->key;
+        p.row_base = m->vocab_lo;
+        VRT_TRY(gemv(kProResidFinal, kEpiArgmax, p));
+        if (m->world > 1) {
+            const int r = m->nccl.AllReduce(&m->st->key, &m->st->key, 1, /*ncclUint64*/ 5, /*ncclMax*/ 2, m->comm, s);
+            if (r) return fail(VRT_E_CUDA, "ncclAllReduce(max) failed: %s", m->nccl.GetErrorString(r));
+        }
+        VRT_CUDA(launch(finalize_decode_kernel, dim3(1), dim3(1), 0, s, pdl && m->world <= 1, m->st,
+                        c.vocab_size, m->out_ids, kMaxSteps));
+        nk += 1;
+    } else {
+        VRT_CUDA(launch(final_hidden_kernel, dim3(1), dim3(1024), d * 4, s, pdl, (const float*)m->dn,
+                        (const float*)m->h1, F(last.n_post_ffw), F(m->out_norm), m->hidden, tlast, d, c.rms_epsilon,
+                        status));
+        VRT_CUDA(launch(finalize_prefill_kernel, dim3(1), dim3(1), 0, s, pdl, m->st, (const uint32_t*)m->prompt));
+        nk += 2;
+    }
+    if (kernels) *kernels = nk;
+    return VRT_OK;
+}
+
+static int build_graphs(vrt_model* m) {
+    if (!m->opt.use_graph) return VRT_OK;
+    for (int head = 0; head < 2; ++head) {
+        cudaGraph_t g = nullptr;
+        cudaStream_t s = m->ctx->stream;
+        VRT_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        uint32_t nk = 0;
+        const int rc = record_step(m, s, head != 0, &nk);
+        const cudaError_t e = cudaStreamEndCapture(s, &g);
+        if (rc != VRT_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture", __FILE__, __LINE__);
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t ei = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) return cuda_fail(ei, "cudaGraphInstantiate", __FILE__, __LINE__);
+        (head ? m->g_head : m->g_nohead) = ex;
+        if (head) m->kernels_per_step = nk;
+    }
+    return VRT_OK;
+}
+
+static int run_step(vrt_model* m, bool head) {
+    cudaStream_t s = m->ctx->stream;
+    cudaGraphExec_t ex = head ? m->g_head : m->g_nohead;
+    if (ex) {
+        VRT_CUDA(cudaGraphLaunch(ex, s));
+        return VRT_OK;
+    }
+    return record_step(m, s, head, nullptr);
+}
+
+static int finish_create(vrt_model* m) {
+    if (m->world > 1) {
+        VRT_TRY(nccl_load(m->nccl));
+        auto init = reinterpret_cast<CommInitRankFn>(dlsym(m->nccl.lib, "ncclCommInitRank"));
+        if (!init) return fail(VRT_E_UNSUPPORTED, "ncclCommInitRank missing");
+        NcclId id;
+        memcpy(id.b, m->opt.nccl_id, 128);
+        const int r = init(&m->comm, m->world, id, m->rank);
+        if (r) return fail(VRT_E_CUDA, "ncclCommInitRank failed: %s", m->nccl.GetErrorString(r));
+    }
+    VRT_TRY(build_graphs(m));
+    return VRT_OK;
+}
+
+static void destroy_model(vrt_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->g_head) cudaGraphExecDestroy(m->g_head);
+    if (m->g_nohead) cudaGraphExecDestroy(m->g_nohead);
+    if (m->comm && m->nccl.CommDestroy) m->nccl.CommDestroy(m->comm);
+    cudaFree(m->arena);
+    cudaFree(m->kv_mem);
+    cudaFree(m->rope_cos_l);
+    cudaFree(m->act_mem);
+    cudaFree(m->tickets);
+    cudaFree(m->out_ids);
+    cudaFree(m->prompt);
+    cudaFree(m->st);
+    cudaFree(m->key_tmp);
+    if (m->st_host) cudaFreeHost(m->st_host);
+    if (m->hidden_host) cudaFreeHost(m->hidden_host);
+    delete m;
+}
+
+static int begin_model(vrt_ctx* ctx, const vrt_model_options* opts, vrt_model** out, std::unique_ptr<vrt_model>& m) {
+    if (!ctx || !out) return fail(VRT_E_INVALID, "null argument");
+    m.reset(new vrt_model());
+    m->ctx = ctx;
+    vrt_model_options_default(&m->opt);
+    if (opts) m->opt = *opts;
+    m->world = m->opt.tp_world > 1 ? m->opt.tp_world : 1;
+    m->rank = m->world > 1 ? m->opt.tp_rank : 0;
+    if (m->world > 1 && (m->rank < 0 || m->rank >= m->world || !m->opt.nccl_id)) {
+        return fail(VRT_E_INVALID, "tensor-parallel rank/world/nccl_id invalid");
+    }
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    VRT_CUDA(gemv_init_attributes());
+    return VRT_OK;
+}
+
+static int device_status(vrt_model* m, uint32_t& status) {
+    status = m->st_host->status;
+    if (!status) return VRT_OK;
+    const char* what = (status & kStatusWaitTimeout) ? "a bounded device wait timed out"
+                       : (status & kStatusBadToken)  ? "Token id is outside Gemma 3 vocabulary"
+                                                     : "Non-finite value in the Gemma 3 hidden state or logits";
+    return fail((status & kStatusWaitTimeout) ? VRT_E_TIMEOUT : VRT_E_NUMERIC, "%s (device status 0x%x)", what, status);
+}
+
+}  // namespace vrt
+
+using namespace vrt;
+
+extern "C" {
+
+void vrt_model_options_default(vrt_model_options* o) {
+    if (!o) return;
+    memset(o, 0, sizeof *o);
+    o->use_graph = 1;
+    o->use_pdl = 1;
+}
+
+int vrt_model_load(vrt_ctx* ctx, const char* path, const vrt_model_options* opts, vrt_model** out) {
+    clear_error();
+    std::unique_ptr<vrt_model> m;
+    VRT_TRY(begin_model(ctx, opts, out, m));
+    if (!path) return fail(VRT_E_INVALID, "null path");
+    try {
+        vortexrt::GgufFile g(path);
+        VRT_TRY(read_config(g, m->cfg, m->eos));
+        VRT_TRY(plan(m.get()));
+        VRT_TRY(alloc_runtime(m.get()));
+        const int rc = load_weights(m.get(), g);
+        if (rc != VRT_OK) {
+            destroy_model(m.release());
+            return rc;
+        }
+    } catch (const std::exception& e) {
+        vrt_model* raw = m.release();
+        if (raw && raw->arena) destroy_model(raw); else delete raw;
+        return fail(VRT_E_IO, "%s", e.what());
+    }
+    const int rc = finish_create(m.get());
+    if (rc != VRT_OK) {
+        destroy_model(m.release());
+        return rc;
+    }
+    *out = m.release();
+    return VRT_OK;
+}
+
+int vrt_model_create_synthetic(vrt_ctx* ctx, const vrt_gemma3_config* cfg, uint64_t seed,
+                               const vrt_model_options* opts, vrt_model** out) {
+    clear_error();
+    std::unique_ptr<vrt_model> m;
+    VRT_TRY(begin_model(ctx, opts, out, m));
+    if (!cfg) return fail(VRT_E_INVALID, "null config");
+    m->cfg = *cfg;
+    m->cfg.value_dim = m->cfg.value_dim ? m->cfg.value_dim : m->cfg.head_dim;
+    if (m->cfg.local_rope_base == 0.0f) m->cfg.local_rope_base = 1.0e4f;
+    if (m->cfg.global_rope_base == 0.0f) m->cfg.global_rope_base = 1.0e6f;
+    if (m->cfg.rms_epsilon == 0.0f) m->cfg.rms_epsilon = 1e-6f;
+    VRT_TRY(validate_config(m->cfg));
+    VRT_TRY(plan(m.get()));
+    int rc = alloc_runtime(m.get());
+    if (rc == VRT_OK) rc = synth_weights(m.get(), seed);
+    if (rc == VRT_OK) rc = finish_create(m.get());
+    if (rc != VRT_OK) {
+        destroy_model(m.release());
+        return rc;
+    }
+    *out = m.release();
+    return VRT_OK;
+}
+
+int vrt_model_destroy(vrt_model* m) {
+    destroy_model(m);
+    return VRT_OK;
+}
+
+int vrt_model_config(vrt_model* m, vrt_gemma3_config* out) {
+    if (!m || !out) return fail(VRT_E_INVALID, "null argument");
+    *out = m->cfg;
+    return VRT_OK;
+}
+
+int vrt_model_reset(vrt_model* m) {
+    if (!m) return fail(VRT_E_INVALID, "null model");
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    memset(m->st_host, 0, sizeof(StepState));
+    VRT_CUDA(cudaMemcpyAsync(m->st, m->st_host, sizeof(StepState), cudaMemcpyHostToDevice, m->ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    m->next_pos = 0;
+    m->generated = 0;
+    return VRT_OK;
+}
+
+int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t top_k, float* h_hidden,
+                    uint32_t* h_ids, float* h_logits) {
+    clear_error();
+    if (!m) return fail(VRT_E_INVALID, "null model");
+    const auto& c = m->cfg;
+    if (position != m->next_pos) return fail(VRT_E_STATE, "Gemma 3 decode positions must be contiguous");
+    if (position >= c.context_length) return fail(VRT_E_STATE, "Gemma 3 context length exceeded");
+    if (position >= m->P) return fail(VRT_E_STATE, "position %u exceeds the allocated KV capacity %u", position, m->P);
+    if (token >= c.vocab_size) {
+        vrt_model_reset(m);
+        return fail(VRT_E_INVALID, "Token id is outside Gemma 3 vocabulary");
+    }
+    if (top_k > 1 && m->world > 1) return fail(VRT_E_UNSUPPORTED, "top_k > 1 is not available with tensor parallelism");
+    cudaStream_t s = m->ctx->stream;
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    StepState* sh = m->st_host;
+    sh->token = token;
+    sh->pos = position;
+    sh->status = 0;
+    sh->prompt_count = 0;
+    VRT_CUDA(cudaMemcpyAsync(m->st, sh, 20, cudaMemcpyHostToDevice, s));
+    VRT_TRY(run_step(m, top_k > 0));
+    VRT_CUDA(cudaMemcpyAsync(sh, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, s));
+    if (h_hidden) VRT_CUDA(cudaMemcpyAsync(m->hidden_host, m->hidden, 4ull * c.embedding_length, cudaMemcpyDeviceToHost, s));
+    std::vector<float> logits;
+    if (top_k > 1) {
+        logits.resize(c.vocab_size);
+        VRT_CUDA(cudaMemcpyAsync(logits.data(), m->logits, 4ull * c.vocab_size, cudaMemcpyDeviceToHost, s));
+    }
+    VRT_CUDA(cudaStreamSynchronize(s));
+    uint32_t status;
+    if (const int rc = device_status(m, status); rc != VRT_OK) {
+        vrt_model_reset(m);
+        return rc;
+    }
+    if (h_hidden) memcpy(h_hidden, m->hidden_host, 4ull * c.embedding_length);
+    if (top_k == 1) {
+        if (sh->result_index >= c.vocab_size || !std::isfinite(sh->result_value)) {
+            vrt_model_reset(m);
+            return fail(VRT_E_NUMERIC, "GPU argmax produced invalid result");
+        }
+        if (h_ids) h_ids[0] = sh->result_index;
+        if (h_logits) h_logits[0] = sh->result_value;
+    } else if (top_k > 1) {
+        const uint32_t k = std::min(top_k, c.vocab_size);
+        std::vector<uint32_t> ids(c.vocab_size);
+        for (uint32_t i = 0; i < c.vocab_size; ++i) ids[i] = i;
+        std::partial_sort(ids.begin(), ids.begin() + k, ids.end(), [&](uint32_t a, uint32_t b) {
+            return logits[a] > logits[b] || (logits[a] == logits[b] && a < b);
+        });
+        for (uint32_t i = 0; i < k; ++i) {
+            if (!std::isfinite(logits[ids[i]])) {
+                vrt_model_reset(m);
+                return fail(VRT_E_NUMERIC, "Non-finite Gemma 3 logit");
+            }
+            if (h_ids) h_ids[i] = ids[i];
+            if (h_logits) h_logits[i] = logits[ids[i]];
+        }
+    }
+    m->next_pos = position + 1;
+    return VRT_OK;
+}
+
+int vrt_model_logits(vrt_model* m, float* h_logits) {
+    if (!m || !h_logits) return fail(VRT_E_INVALID, "null argument");
+    const uint32_t n = m->vocab_hi - m->vocab_lo;
+    VRT_CUDA(cudaMemcpy(h_logits, m->logits, 4ull * n, cudaMemcpyDeviceToHost));
+    return VRT_OK;
+}
+
+int vrt_prefill(vrt_model* m, const uint32_t* h_prompt, uint32_t n) {
+    clear_error();
+    if (!m || (!h_prompt && n)) return fail(VRT_E_INVALID, "null argument");
+    if (n == 0) return fail(VRT_E_INVALID, "Gemma 3 prompt produced no input tokens");
+    const auto& c = m->cfg;
+    if (n > m->P || n > c.context_length) return fail(VRT_E_STATE, "prompt of %u tokens exceeds capacity %u", n, m->P);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (h_prompt[i] >= c.vocab_size) return fail(VRT_E_INVALID, "Token id is outside Gemma 3 vocabulary");
+    }
+    cudaStream_t s = m->ctx->stream;
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    VRT_CUDA(cudaMemcpyAsync(m->prompt, h_prompt, 4ull * n, cudaMemcpyHostToDevice, s));
+    StepState* sh = m->st_host;
+    memset(sh, 0, sizeof(StepState));
+    sh->token = h_prompt[0];
+    sh->prompt_count = n;
+    VRT_CUDA(cudaMemcpyAsync(m->st, sh, sizeof(StepState), cudaMemcpyHostToDevice, s));
+    for (uint32_t i = 0; i + 1 < n; ++i) VRT_TRY(run_step(m, false));
+    VRT_TRY(run_step(m, true));
+    VRT_CUDA(cudaMemcpyAsync(sh, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    uint32_t status;
+    if (const int rc = device_status(m, status); rc != VRT_OK) {
+        vrt_model_reset(m);
+        return rc;
+    }
+    m->next_pos = n;
+    m->generated = 1;
+    return VRT_OK;
+}
+
+int vrt_decode_steps_async(vrt_model* m, uint32_t steps, uint32_t* d_out_ids, void* stream) {
+    if (!m) return fail(VRT_E_INVALID, "null model");
+    if (m->next_pos + steps > m->P || m->next_pos + steps > m->cfg.context_length) {
+        return fail(VRT_E_STATE, "decode would exceed the KV capacity");
+    }
+    if (m->generated + steps > kMaxSteps) return fail(VRT_E_STATE, "more than %u generated ids since the prefill", kMaxSteps);
+    cudaStream_t s = m->ctx->stream;
+    if (stream && stream != s) {
+        // order the steps after the caller's stream
+        cudaEvent_t ev;
+        VRT_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        VRT_CUDA(cudaEventRecord(ev, static_cast<cudaStream_t>(stream)));
+        VRT_CUDA(cudaStreamWaitEvent(s, ev, 0));
+        VRT_CUDA(cudaEventDestroy(ev));
+    }
+    for (uint32_t i = 0; i < steps; ++i) VRT_TRY(run_step(m, true));
+    const uint32_t first = m->generated;
+    m->generated += steps;
+    m->next_pos += steps;
+    if (d_out_ids) {
+        VRT_CUDA(cudaMemcpyAsync(d_out_ids, m->out_ids + first, 4ull * steps, cudaMemcpyDeviceToDevice, s));
+    }
+    if (stream && stream != s) {
+        cudaEvent_t ev;
+        VRT_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        VRT_CUDA(cudaEventRecord(ev, s));
+        VRT_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), ev, 0));
+        VRT_CUDA(cudaEventDestroy(ev));
+    }
+    return VRT_OK;
+}
+
+int vrt_model_next_token(vrt_model* m, uint32_t* h_token, uint32_t* h_position) {
+    if (!m) return fail(VRT_E_INVALID, "null model");
+    VRT_CUDA(cudaMemcpyAsync(m->st_host, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, m->ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (h_token) *h_token = m->st_host->token;
+    if (h_position) *h_position = m->st_host->pos;
+    return VRT_OK;
+}
+
+int vrt_generate_greedy(vrt_model* m, const uint32_t* h_prompt, uint32_t n, uint32_t max_new, uint32_t* h_out,
+                        uint32_t* h_count) {
+    clear_error();
+    if (!m || !h_count || (max_new && !h_out)) return fail(VRT_E_INVALID, "null argument");
+    *h_count = 0;
+    VRT_TRY(vrt_model_reset(m));
+    if (max_new == 0) return VRT_OK;
+    if (max_new > kMaxSteps) return fail(VRT_E_INVALID, "max_new above %u", kMaxSteps);
+    if (static_cast<uint64_t>(n) + max_new - 1 > m->P) return fail(VRT_E_STATE, "generation exceeds the KV capacity");
+    VRT_TRY(vrt_prefill(m, h_prompt, n));  // emits generated id 0
+    if (max_new > 1) VRT_TRY(vrt_decode_steps_async(m, max_new - 1, nullptr, nullptr));
+    std::vector<uint32_t> ids(max_new);
+    VRT_CUDA(cudaMemcpyAsync(ids.data(), m->out_ids, 4ull * max_new, cudaMemcpyDeviceToHost, m->ctx->stream));
+    VRT_CUDA(cudaMemcpyAsync(m->st_host, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, m->ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    uint32_t status;
+    if (const int rc = device_status(m, status); rc != VRT_OK) {
+        vrt_model_reset(m);
+        return rc;
+    }
+    uint32_t cnt = 0;
+    for (uint32_t i = 0; i < max_new; ++i) {
+        h_out[cnt++] = ids[i];
+        if (ids[i] == m->eos) break;  // gemma3.cpp:2139-2141
+    }
+    *h_count = cnt;
+    return VRT_OK;
+}
+
+int vrt_model_step_kernels(vrt_model* m, uint32_t* out) {
+    if (!m || !out) return fail(VRT_E_INVALID, "null argument");
+    if (!m->kernels_per_step) {
+        // count by recording into a throw-away capture
+        cudaGraph_t g = nullptr;
+        VRT_CUDA(cudaStreamBeginCapture(m->ctx->stream, cudaStreamCaptureModeThreadLocal));
+        uint32_t nk = 0;
+        record_step(m, m->ctx->stream, true, &nk);
+        cudaStreamEndCapture(m->ctx->stream, &g);
+        if (g) cudaGraphDestroy(g);
+        m->kernels_per_step = nk;
+    }
+    *out = m->kernels_per_step;
+    return VRT_OK;
+}
+
+int vrt_model_device_status(vrt_model* m, uint32_t* h_status) {
+    if (!m || !h_status) return fail(VRT_E_INVALID, "null argument");
+    VRT_CUDA(cudaMemcpyAsync(m->st_host, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, m->ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    *h_status = m->st_host->status;
+    return VRT_OK;
+}
+
+int vrt_model_set_trace(vrt_model* m, int enabled) {
+    if (!m) return fail(VRT_E_INVALID, "null model");
+    if ((enabled != 0) == m->trace_on) return VRT_OK;
+    m->trace_on = enabled != 0;
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    if (m->g_head) cudaGraphExecDestroy(m->g_head);
+    if (m->g_nohead) cudaGraphExecDestroy(m->g_nohead);
+    m->g_head = m->g_nohead = nullptr;
+    return build_graphs(m);
+}
+
+int vrt_model_trace(vrt_model* m, float* h_out) {
+    if (!m || !h_out) return fail(VRT_E_INVALID, "null argument");
+    VRT_CUDA(cudaMemcpy(h_out, m->trace, 4ull * m->cfg.block_count * m->cfg.embedding_length, cudaMemcpyDeviceToHost));
+    return VRT_OK;
+}
+
+// ----------------------------------------------- packed (Q8T) fast path
+
+uint64_t vrt_q8t_bytes(uint32_t rows, uint32_t cols) { return q8t_bytes(rows, cols); }
+
+static int check_packable(vrt_ctx* ctx, uint64_t raw_bytes, uint64_t off, uint32_t rows, uint32_t cols) {
+    if (!ctx) return fail(VRT_E_INVALID, "null context");
+    if (!rows || !cols || cols % 128) return fail(VRT_E_INVALID, "packed Q8_0 needs rows > 0 and cols %% 128 == 0");
+    const uint64_t bytes = static_cast<uint64_t>(rows) * (cols / 32) * 34;
+    if (off > raw_bytes || bytes > raw_bytes - off) return fail(VRT_E_INVALID, "raw weight buffer is too small");
+    return VRT_OK;
+}
+
+int vrt_q8t_pack(vrt_ctx* ctx, const void* d_raw, uint64_t raw_bytes, uint64_t off, uint32_t rows, uint32_t cols,
+                 void* d_packed, void* stream) {
+    clear_error();
+    VRT_TRY(check_packable(ctx, raw_bytes, off, rows, cols));
+    if (!d_raw || !d_packed) return fail(VRT_E_INVALID, "null buffer");
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaMemsetAsync(d_packed, 0, q8t_bytes(rows, cols), s));
+    RepackParams p{static_cast<const uint8_t*>(d_raw) + off, static_cast<uint64_t>(cols) / 32 * 34, 0, rows,
+                   cols / 32, static_cast<uint8_t*>(d_packed), cols, 0, 0};
+    const uint64_t work = static_cast<uint64_t>(rows) * (cols / 32);
+    VRT_CUDA(launch(repack_kernel, dim3(static_cast<unsigned>((work + 255) / 256)), dim3(256), 0, s, false, p));
+    return VRT_OK;
+}
+
+int vrt_q8t_pack_pair(vrt_ctx* ctx, const void* d_raw, uint64_t raw_bytes, uint64_t gate_off, uint64_t up_off,
+                      uint32_t ffn, uint32_t cols, void* d_packed, void* stream) {
+    clear_error();
+    VRT_TRY(check_packable(ctx, raw_bytes, gate_off, ffn, cols));
+    VRT_TRY(check_packable(ctx, raw_bytes, up_off, ffn, cols));
+    if (ffn % 8) return fail(VRT_E_INVALID, "gate/up rows must be a multiple of 8");
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaMemsetAsync(d_packed, 0, q8t_bytes(2ull * ffn, cols), s));
+    for (int mode = 1; mode <= 2; ++mode) {
+        RepackParams p{static_cast<const uint8_t*>(d_raw) + (mode == 1 ? gate_off : up_off),
+                       static_cast<uint64_t>(cols) / 32 * 34, 0, ffn, cols / 32, static_cast<uint8_t*>(d_packed), cols,
+                       0, mode};
+        const uint64_t work = static_cast<uint64_t>(ffn) * (cols / 32);
+        VRT_CUDA(launch(repack_kernel, dim3(static_cast<unsigned>((work + 255) / 256)), dim3(256), 0, s, false, p));
+    }
+    return VRT_OK;
+}
+
+static int packed_gemv(vrt_ctx* ctx, int pro, int epi, GemvParams& p, cudaStream_t s) {
+    static uint32_t* status = nullptr;
+    if (!status) VRT_CUDA(cudaMalloc(&status, 4));
+    p.status = status;
+    if (p.eps == 0.0f) p.eps = 1e-6f;
+    VRT_CUDA(gemv_init_attributes());
+    VRT_CUDA(gemv_q8t(pro, epi, p, gemv_grid(ctx->prop.multiProcessorCount, p.rows), s, false));
+    return VRT_OK;
+}
+
+int vrt_q8t_gemv(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint32_t cols, const float* d_x, float* d_y,
+                 void* stream) {
+    clear_error();
+    if (!ctx || !d_packed || !d_x || !d_y) return fail(VRT_E_INVALID, "null argument");
+    if (!rows || !cols || cols % 128) return fail(VRT_E_INVALID, "packed Q8_0 needs rows > 0 and cols %% 128 == 0");
+    if (reinterpret_cast<uintptr_t>(d_packed) % 16) return fail(VRT_E_INVALID, "packed weights must be 16-byte aligned");
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaMemsetAsync(d_y, 0, 4ull * rows, s));
+    GemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_packed);
+    p.rows = rows;
+    p.cols = cols;
+    p.x = d_x;
+    p.y = d_y;
+    return packed_gemv(ctx, kProPlain, kEpiAtomic, p, s);
+}
+
+int vrt_q8t_gate_up(vrt_ctx* ctx, const void* d_packed_pair, uint32_t ffn, uint32_t cols, const float* d_x,
+                    float* d_act, void* stream) {
+    clear_error();
+    if (!ctx || !d_packed_pair || !d_x || !d_act) return fail(VRT_E_INVALID, "null argument");
+    if (!ffn || ffn % 8 || !cols || cols % 128) return fail(VRT_E_INVALID, "gate/up shape unsupported");
+    if (reinterpret_cast<uintptr_t>(d_packed_pair) % 16) return fail(VRT_E_INVALID, "packed weights must be 16-byte aligned");
+    GemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_packed_pair);
+    p.rows = 2 * ffn;
+    p.cols = cols;
+    p.x = d_x;
+    p.y = d_act;
+    return packed_gemv(ctx, kProPlain, kEpiGeluPair, p, as_stream(ctx, stream));
+}
+
+int vrt_q8t_ffn(vrt_ctx* ctx, const void* d_gate_up, const void* d_down, uint32_t input_dim, uint32_t ffn_dim,
+                uint32_t output_dim, const float* d_x, float* d_act, float* d_y, void* stream) {
+    VRT_TRY(vrt_q8t_gate_up(ctx, d_gate_up, ffn_dim, input_dim, d_x, d_act, stream));
+    return vrt_q8t_gemv(ctx, d_down, output_dim, ffn_dim, d_act, d_y, stream);
+}
+
+int vrt_q8t_lm_head_argmax(vrt_ctx* ctx, const void* d_packed, uint32_t vocab, uint32_t cols, const float* d_x,
+                           float* d_logits, vrt_argmax_result* d_out, void* stream) {
+    clear_error();
+    if (!ctx || !d_packed || !d_x || !d_out) return fail(VRT_E_INVALID, "null argument");
+    if (!vocab || !cols || cols % 128) return fail(VRT_E_INVALID, "packed Q8_0 needs rows > 0 and cols %% 128 == 0");
+    if (reinterpret_cast<uintptr_t>(d_packed) % 16) return fail(VRT_E_INVALID, "packed weights must be 16-byte aligned");
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaMemsetAsync(ctx->d_key, 0, 8, s));
+    GemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_packed);
+    p.rows = vocab;
+    p.cols = cols;
+    p.x = d_x;
+    p.y = d_logits;
+    p.amax = ctx->d_key;
+    VRT_TRY(packed_gemv(ctx, kProPlain, kEpiArgmax, p, s));
+    VRT_CUDA(argmax_unkey_launch(ctx->d_key, reinterpret_cast<uint32_t*>(d_out), s));
+    return VRT_OK;
+}
+
+// Time one of the step's mat-vec launches in isolation (same kernel and
+// parameters as inside the step, no PDL), on the model stream, between CUDA
+// events.  which: 0 qkv, 1 o-proj, 2 gate/up, 3 down, 4 LM head.  Clobbers
+// activations: call vrt_model_reset before decoding again.
+int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, uint32_t iters, float* ms_per_launch,
+                          uint64_t* algorithmic_bytes) {
+    clear_error();
+    if (!m || !ms_per_launch || which > 4 || layer >= m->cfg.block_count || iters == 0) {
+        return fail(VRT_E_INVALID, "bad argument");
+    }
+    const auto& c = m->cfg;
+    const auto& L = m->layers[layer];
+    const uint32_t d = c.embedding_length;
+    auto F = [&](uint64_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+    GemvParams p{};
+    int pro = kProPlain, epi = kEpiAtomic;
+    uint64_t vec_bytes = 0;
+    p.status = &m->st->status;
+    p.eps = c.rms_epsilon;
+    switch (which) {
+    case 0:
+        p.w = m->arena + L.qkv; p.rows = m->qwl + 2 * m->kwl; p.cols = d;
+        p.x = m->dn; p.h_prev = m->h1; p.w_post = F(L.n_post_ffw); p.w_pre = F(L.n_attn); p.h_out = m->h0; p.y = m->qkv;
+        pro = kProResid;
+        vec_bytes = 4ull * (5 * d + p.rows);
+        break;
+    case 1:
+        p.w = m->arena + L.o; p.rows = d; p.cols = m->qwl; p.x = m->att; p.y = m->o;
+        vec_bytes = 4ull * (p.cols + d);
+        break;
+    case 2:
+        p.w = m->arena + L.gu; p.rows = 2 * m->ffl; p.cols = d;
+        p.x = m->o; p.h_prev = m->h0; p.w_post = F(L.n_post_attn); p.w_pre = F(L.n_ffn); p.h_out = m->h1; p.y = m->act;
+        pro = kProResid; epi = kEpiGeluPair;
+        vec_bytes = 4ull * (5 * d + m->ffl);
+        break;
+    case 3:
+        p.w = m->arena + L.down; p.rows = d; p.cols = m->ffl; p.x = m->act; p.y = m->dn;
+        vec_bytes = 4ull * (m->ffl + d);
+        break;
+    default: {
+        const uint32_t kt = d / kTileCols;
+        p.w = m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes;
+        p.rows = m->vocab_hi - m->vocab_lo; p.cols = d;
+        p.x = m->dn; p.h_prev = m->h1; p.w_post = F(L.n_post_ffw); p.w_pre = F(m->out_norm); p.h_out = m->hidden;
+        p.y = m->logits; p.amax = m->key_tmp; p.row_base = m->vocab_lo;
+        pro = kProResidFinal; epi = kEpiArgmax;
+        vec_bytes = 4ull * (4 * d + 2 * d + p.rows);
+    }
+    }
+    const uint64_t wbytes = q8t_bytes(p.rows, p.cols);
+    if (algorithmic_bytes) *algorithmic_bytes = static_cast<uint64_t>(p.rows) * (p.cols / 32) * 34 + vec_bytes;
+    (void)wbytes;
+    cudaStream_t s = m->ctx->stream;
+    const int grid = gemv_grid(m->ctx->prop.multiProcessorCount, p.rows);
+    cudaEvent_t e0, e1;
+    VRT_CUDA(cudaEventCreate(&e0));
+    VRT_CUDA(cudaEventCreate(&e1));
+    VRT_CUDA(gemv_q8t(pro, epi, p, grid, s, false));  // warm
+    VRT_CUDA(cudaEventRecord(e0, s));
+    for (uint32_t i = 0; i < iters; ++i) VRT_CUDA(gemv_q8t(pro, epi, p, grid, s, false));
+    VRT_CUDA(cudaEventRecord(e1, s));
+    VRT_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.0f;
+    VRT_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_per_launch = ms / static_cast<float>(iters);
+    return VRT_OK;
+}
+
+int vrt_tp_unique_id(void* h_out128) {
+    clear_error();
+    if (!h_out128) return fail(VRT_E_INVALID, "null argument");
+    static Nccl n;
+    VRT_TRY(nccl_load(n));
+    const int r = n.GetUniqueId(h_out128);
+    if (r) return fail(VRT_E_CUDA, "ncclGetUniqueId failed: %s", n.GetErrorString(r));
+    return VRT_OK;
+}
+
+}  // extern "C"

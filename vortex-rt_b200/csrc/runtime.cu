@@ -1,0 +1,400 @@
+// Runtime layer of the C ABI: device context, allocation and copies (the
+// role of the reference's VulkanContext/Buffer, src/vulkan_context.cpp and
+// src/buffer.cpp), the Q8_0 pipeline entry points over raw GGUF rows (the
+// role of Q8MatVecPipeline / ArgmaxPipeline), the packed (Q8T) fast path,
+// and the kernel dispatch tables used by the model.
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+#include "attention.cuh"
+#include "gemv_q8t.cuh"
+#include "pipeline_kernels.cuh"
+#include "vrt_internal.hpp"
+#include "vrt_kernels.hpp"
+
+namespace vrt {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int cuda_fail(cudaError_t e, const char* what, const char* file, int line) {
+    const char* base = strrchr(file, '/');
+    return fail(e == cudaErrorMemoryAllocation ? VRT_E_NOMEM : VRT_E_CUDA, "%s failed: %s (%s:%d)", what,
+                cudaGetErrorString(e), base ? base + 1 : file, line);
+}
+
+int check_device_ptr(vrt_ctx* ctx, const void* p, const char* what) {
+    if (!p) return fail(VRT_E_INVALID, "%s is null", what);
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(VRT_E_INVALID, "%s is not a CUDA pointer", what);
+    }
+    if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) {
+        return fail(VRT_E_INVALID, "%s is not device memory", what);
+    }
+    if (a.device != ctx->device) return fail(VRT_E_INVALID, "%s lives on another device", what);
+    return VRT_OK;
+}
+
+// ----------------------------------------------------------- dispatch
+
+template <int PRO, int EPI>
+static cudaError_t gemv_launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+    const uint32_t smem = gemv_smem_layout(p.cols, PRO).total;
+    return launch(q8t_gemv_kernel<PRO, EPI>, dim3(grid), dim3(kGemvThreads), smem, s, pdl, p);
+}
+
+template <int PRO, int EPI>
+static cudaError_t gemv_attr_t() {
+    return cudaFuncSetAttribute(q8t_gemv_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+// Raise the dynamic shared-memory limit of every instantiation once, before
+// any stream capture.
+cudaError_t gemv_init_attributes() {
+    cudaError_t e = cudaSuccess;
+#define VRT_GA(P, E) if (e == cudaSuccess) e = gemv_attr_t<P, E>();
+    VRT_GA(kProPlain, kEpiAtomic)
+    VRT_GA(kProRmsInto, kEpiAtomic)
+    VRT_GA(kProEmbed, kEpiAtomic)
+    VRT_GA(kProResid, kEpiAtomic)
+    VRT_GA(kProResid, kEpiGeluPair)
+    VRT_GA(kProPlain, kEpiGeluPair)
+    VRT_GA(kProRmsInto, kEpiGeluPair)
+    VRT_GA(kProResidFinal, kEpiArgmax)
+    VRT_GA(kProPlain, kEpiArgmax)
+    VRT_GA(kProRmsInto, kEpiArgmax)
+#undef VRT_GA
+    return e;
+}
+
+cudaError_t gemv_q8t(int pro, int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
+#define VRT_G(P, E)                                 \
+    if (pro == P && epi == E) return gemv_launch_t<P, E>(p, grid, s, pdl);
+    VRT_G(kProPlain, kEpiAtomic)
+    VRT_G(kProRmsInto, kEpiAtomic)
+    VRT_G(kProEmbed, kEpiAtomic)
+    VRT_G(kProResid, kEpiAtomic)
+    VRT_G(kProResid, kEpiGeluPair)
+    VRT_G(kProPlain, kEpiGeluPair)
+    VRT_G(kProRmsInto, kEpiGeluPair)
+    VRT_G(kProResidFinal, kEpiArgmax)
+    VRT_G(kProPlain, kEpiArgmax)
+    VRT_G(kProRmsInto, kEpiArgmax)
+#undef VRT_G
+    return cudaErrorInvalidValue;
+}
+
+uint32_t gemv_smem_bytes(int pro, uint32_t cols) { return gemv_smem_layout(cols, pro).total; }
+
+cudaError_t argmax_unkey_launch(const unsigned long long* key, uint32_t* out, cudaStream_t s) {
+    return launch(argmax_unkey_kernel, dim3(1), dim3(1), 0, s, false, key, out);
+}
+
+cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl) {
+    const uint32_t M = p.hd / 32, R = p.H / p.KV;
+    const int rg = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
+#define VRT_A(MM, RR) \
+    if (M == MM && rg == RR) return launch(attention_decode_kernel<MM, RR>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+    VRT_A(2, 1) VRT_A(2, 2) VRT_A(2, 4) VRT_A(2, 8)
+    VRT_A(4, 1) VRT_A(4, 2) VRT_A(4, 4) VRT_A(4, 8)
+    VRT_A(8, 1) VRT_A(8, 2) VRT_A(8, 4) VRT_A(8, 8)
+#undef VRT_A
+    return cudaErrorInvalidValue;
+}
+
+static int raw_gemv(vrt_ctx* ctx, const RawGemvParams& p, cudaStream_t s) {
+    const uint32_t nblk = p.cols / 32;
+    const uint32_t smem = ((nblk * 4 + 15) / 16) * 16 + p.cols * 2;
+    const uint32_t rows = p.row_start[p.count];
+    const int G = nblk <= 32 ? 8 : (nblk <= 64 ? 16 : 32);
+    const uint32_t rows_per_cta = (kRawThreads / 32) * (32 / G);
+    int occ = 2;
+    const uint32_t max_grid = static_cast<uint32_t>(ctx->prop.multiProcessorCount) * occ;
+    const uint32_t grid = std::max(1u, std::min(max_grid, (rows + rows_per_cta - 1) / rows_per_cta));
+    static bool attr[3] = {false, false, false};
+    void (*k)(const RawGemvParams) = G == 8 ? raw_gemv_kernel<8> : (G == 16 ? raw_gemv_kernel<16> : raw_gemv_kernel<32>);
+    const int ai = G == 8 ? 0 : (G == 16 ? 1 : 2);
+    if (!attr[ai]) {
+        VRT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr[ai] = true;
+    }
+    if (smem > 227u * 1024u) return fail(VRT_E_UNSUPPORTED, "input_dim %u too large for one CTA", p.cols);
+    VRT_CUDA(launch(k, dim3(grid), dim3(kRawThreads), smem, s, false, p));
+    return VRT_OK;
+}
+
+static int check_q8_matrix(uint64_t weights_bytes, uint64_t off, uint32_t in, uint32_t out, const char* what) {
+    if (in == 0 || out == 0) return fail(VRT_E_INVALID, "%s dimensions must be non-zero", what);
+    if (in % 32) return fail(VRT_E_INVALID, "%s input_dim must be divisible by 32", what);
+    if (off & 3u) return fail(VRT_E_INVALID, "%s weight byte offset must be 4-byte aligned", what);
+    const uint64_t bytes = static_cast<uint64_t>(in) / 32 * 34 * out;
+    if (off > weights_bytes || bytes > weights_bytes - off) return fail(VRT_E_INVALID, "%s weight buffer is too small", what);
+    return VRT_OK;
+}
+
+}  // namespace vrt
+
+using namespace vrt;
+
+extern "C" {
+
+const char* vrt_last_error(void) { return g_last_error.c_str(); }
+const char* vrt_version(void) { return "vortexrt_b200 0.1 (sm_100a)"; }
+
+int vrt_ctx_create(int device, vrt_ctx** out) {
+    clear_error();
+    if (!out) return fail(VRT_E_INVALID, "out is null");
+    if (device < 0) {
+        const char* env = getenv("VORTEXRT_DEVICE");
+        device = env ? atoi(env) : 0;
+    }
+    int n = 0;
+    VRT_CUDA(cudaGetDeviceCount(&n));
+    if (device >= n) return fail(VRT_E_INVALID, "device %d not present (%d devices)", device, n);
+    auto* c = new vrt_ctx();
+    c->device = device;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaGetDeviceProperties(&c->prop, device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_key, 64);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "vrt_ctx_create", __FILE__, __LINE__);
+    }
+    if (c->prop.major < 10) {
+        const int rc = fail(VRT_E_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device,
+                            c->prop.major, c->prop.minor);
+        cudaFree(c->d_key);
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return VRT_OK;
+}
+
+int vrt_ctx_destroy(vrt_ctx* ctx) {
+    if (!ctx) return VRT_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto& kv : ctx->allocs) cudaFree(kv.first);
+    cudaFree(ctx->d_key);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return VRT_OK;
+}
+
+int vrt_ctx_info(vrt_ctx* ctx, vrt_device_info* out) {
+    if (!ctx || !out) return fail(VRT_E_INVALID, "null argument");
+    memset(out, 0, sizeof *out);
+    strncpy(out->name, ctx->prop.name, sizeof out->name - 1);
+    out->device = ctx->device;
+    out->sm_count = ctx->prop.multiProcessorCount;
+    out->cc_major = ctx->prop.major;
+    out->cc_minor = ctx->prop.minor;
+    out->warp_size = static_cast<uint32_t>(ctx->prop.warpSize);
+    out->global_mem_bytes = ctx->prop.totalGlobalMem;
+    out->l2_bytes = static_cast<uint64_t>(ctx->prop.l2CacheSize);
+    return VRT_OK;
+}
+
+int vrt_ctx_synchronize(vrt_ctx* ctx) {
+    if (!ctx) return fail(VRT_E_INVALID, "null context");
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+    return VRT_OK;
+}
+
+void* vrt_ctx_stream(vrt_ctx* ctx) { return ctx ? ctx->stream : nullptr; }
+
+int vrt_alloc(vrt_ctx* ctx, size_t bytes, void** d_out) {
+    if (!ctx || !d_out) return fail(VRT_E_INVALID, "null argument");
+    if (bytes == 0) return fail(VRT_E_INVALID, "allocation size must be non-zero");
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    void* p = nullptr;
+    VRT_CUDA(cudaMalloc(&p, bytes + 256));
+    VRT_CUDA(cudaMemsetAsync(p, 0, bytes + 256, ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+    std::lock_guard<std::mutex> g(ctx->mu);
+    ctx->allocs[p] = bytes;
+    *d_out = p;
+    return VRT_OK;
+}
+
+int vrt_free(vrt_ctx* ctx, void* d_ptr) {
+    if (!ctx) return fail(VRT_E_INVALID, "null context");
+    if (!d_ptr) return VRT_OK;
+    {
+        std::lock_guard<std::mutex> g(ctx->mu);
+        auto it = ctx->allocs.find(d_ptr);
+        if (it == ctx->allocs.end()) return fail(VRT_E_INVALID, "pointer was not allocated by vrt_alloc");
+        ctx->allocs.erase(it);
+    }
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+    VRT_CUDA(cudaFree(d_ptr));
+    return VRT_OK;
+}
+
+int vrt_upload(vrt_ctx* ctx, void* d_dst, const void* h_src, size_t bytes) {
+    if (!ctx || (!d_dst && bytes) || (!h_src && bytes)) return fail(VRT_E_INVALID, "null argument");
+    if (!bytes) return VRT_OK;
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    VRT_CUDA(cudaMemcpyAsync(d_dst, h_src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+    return VRT_OK;
+}
+
+int vrt_download(vrt_ctx* ctx, void* h_dst, const void* d_src, size_t bytes) {
+    if (!ctx || (!d_src && bytes) || (!h_dst && bytes)) return fail(VRT_E_INVALID, "null argument");
+    if (!bytes) return VRT_OK;
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    VRT_CUDA(cudaMemcpyAsync(h_dst, d_src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+    return VRT_OK;
+}
+
+int vrt_upload_async(vrt_ctx* ctx, void* d_dst, const void* h_src, size_t bytes, void* stream) {
+    if (!ctx) return fail(VRT_E_INVALID, "null context");
+    VRT_CUDA(cudaMemcpyAsync(d_dst, h_src, bytes, cudaMemcpyHostToDevice, as_stream(ctx, stream)));
+    return VRT_OK;
+}
+
+int vrt_download_async(vrt_ctx* ctx, void* h_dst, const void* d_src, size_t bytes, void* stream) {
+    if (!ctx) return fail(VRT_E_INVALID, "null context");
+    VRT_CUDA(cudaMemcpyAsync(h_dst, d_src, bytes, cudaMemcpyDeviceToHost, as_stream(ctx, stream)));
+    return VRT_OK;
+}
+
+int vrt_host_alloc_pinned(size_t bytes, void** h_out) {
+    if (!h_out || !bytes) return fail(VRT_E_INVALID, "bad argument");
+    VRT_CUDA(cudaMallocHost(h_out, bytes));
+    return VRT_OK;
+}
+
+int vrt_host_free_pinned(void* h_ptr) {
+    if (h_ptr) VRT_CUDA(cudaFreeHost(h_ptr));
+    return VRT_OK;
+}
+
+int vrt_q8_gemv(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes, uint64_t off, const float* d_x,
+                float* d_y, uint32_t input_dim, uint32_t output_dim, void* stream) {
+    clear_error();
+    if (!ctx || !d_weights || !d_x || !d_y) return fail(VRT_E_INVALID, "Q8MatVecPipeline: null argument");
+    VRT_TRY(check_q8_matrix(weights_bytes, off, input_dim, output_dim, "Q8MatVecPipeline"));
+    RawGemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_weights);
+    p.offsets[0] = off;
+    p.row_start[0] = 0;
+    p.row_start[1] = output_dim;
+    p.count = 1;
+    p.cols = input_dim;
+    p.x = d_x;
+    p.y = d_y;
+    return raw_gemv(ctx, p, as_stream(ctx, stream));
+}
+
+int vrt_q8_gemv_multi(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes, const uint64_t* offs,
+                      const uint32_t* dims, uint32_t count, const float* d_x, float* d_y, uint32_t input_dim,
+                      void* stream) {
+    clear_error();
+    if (!ctx || !d_weights || !d_x || !d_y || !offs || !dims) return fail(VRT_E_INVALID, "Q8 multi: null argument");
+    if (count == 0 || count > kMaxMulti) return fail(VRT_E_INVALID, "Q8 multi: count must be 1..%d", kMaxMulti);
+    RawGemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_weights);
+    p.count = count;
+    p.cols = input_dim;
+    p.x = d_x;
+    p.y = d_y;
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        VRT_TRY(check_q8_matrix(weights_bytes, offs[i], input_dim, dims[i], "Q8 multi"));
+        p.offsets[i] = offs[i];
+        p.row_start[i] = static_cast<uint32_t>(total);
+        total += dims[i];
+        if (total > 0xffffffffull) return fail(VRT_E_INVALID, "Q8 multi: packed output size overflow");
+    }
+    p.row_start[count] = static_cast<uint32_t>(total);
+    return raw_gemv(ctx, p, as_stream(ctx, stream));
+}
+
+int vrt_gelu_mul(vrt_ctx* ctx, float* d_gate, const float* d_up, uint32_t count, void* stream) {
+    clear_error();
+    if (!ctx || !d_gate || !d_up) return fail(VRT_E_INVALID, "gelu_mul: null argument");
+    if (!count) return VRT_OK;
+    VRT_CUDA(launch(gelu_mul_kernel, dim3((count + 255) / 256), dim3(256), 0, as_stream(ctx, stream), false,
+                    d_gate, d_up, count));
+    return VRT_OK;
+}
+
+int vrt_q8_ffn(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes, uint64_t gate_off, uint64_t up_off,
+               uint64_t down_off, const float* d_x, float* d_ws, float* d_y, uint32_t input_dim, uint32_t ffn_dim,
+               uint32_t output_dim, void* stream) {
+    clear_error();
+    if (!ctx || !d_weights || !d_x || !d_ws || !d_y) return fail(VRT_E_INVALID, "Q8 fused FFN: null argument");
+    if (!input_dim || !ffn_dim || !output_dim || input_dim % 32 || ffn_dim % 32) {
+        return fail(VRT_E_INVALID, "Q8 fused FFN dimensions must be non-zero and Q8 aligned");
+    }
+    VRT_TRY(check_q8_matrix(weights_bytes, gate_off, input_dim, ffn_dim, "Q8 fused FFN gate"));
+    VRT_TRY(check_q8_matrix(weights_bytes, up_off, input_dim, ffn_dim, "Q8 fused FFN up"));
+    VRT_TRY(check_q8_matrix(weights_bytes, down_off, ffn_dim, output_dim, "Q8 fused FFN down"));
+    const uint64_t offs[2] = {gate_off, up_off};
+    const uint32_t dims[2] = {ffn_dim, ffn_dim};
+    VRT_TRY(vrt_q8_gemv_multi(ctx, d_weights, weights_bytes, offs, dims, 2, d_x, d_ws, input_dim, stream));
+    VRT_TRY(vrt_gelu_mul(ctx, d_ws, d_ws + ffn_dim, ffn_dim, stream));
+    return vrt_q8_gemv(ctx, d_weights, weights_bytes, down_off, d_ws, d_y, ffn_dim, output_dim, stream);
+}
+
+int vrt_argmax(vrt_ctx* ctx, const float* d_x, uint32_t count, vrt_argmax_result* d_out, void* stream) {
+    clear_error();
+    if (!ctx || !d_x || !d_out) return fail(VRT_E_INVALID, "ArgmaxPipeline: null argument");
+    if (count == 0) return fail(VRT_E_INVALID, "ArgmaxPipeline requires non-zero input");
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaMemsetAsync(ctx->d_key, 0, 8, s));
+    const uint32_t grid = std::max(1u, std::min((count + 1023) / 1024, static_cast<uint32_t>(ctx->prop.multiProcessorCount) * 4));
+    VRT_CUDA(launch(argmax_kernel, dim3(grid), dim3(1024), 0, s, false, d_x, count, ctx->d_key));
+    VRT_CUDA(launch(argmax_unkey_kernel, dim3(1), dim3(1), 0, s, false, (const unsigned long long*)ctx->d_key,
+                    reinterpret_cast<uint32_t*>(d_out)));
+    return VRT_OK;
+}
+
+int vrt_lm_head_argmax(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes, uint64_t off, const float* d_x,
+                       uint32_t input_dim, uint32_t vocab, float* d_logits, vrt_argmax_result* d_out, void* stream) {
+    clear_error();
+    if (!ctx || !d_weights || !d_x || !d_out) return fail(VRT_E_INVALID, "LM head: null argument");
+    VRT_TRY(check_q8_matrix(weights_bytes, off, input_dim, vocab, "LM head"));
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaMemsetAsync(ctx->d_key, 0, 8, s));
+    RawGemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_weights);
+    p.offsets[0] = off;
+    p.row_start[1] = vocab;
+    p.count = 1;
+    p.cols = input_dim;
+    p.x = d_x;
+    p.y = d_logits;
+    p.amax = ctx->d_key;
+    VRT_TRY(raw_gemv(ctx, p, s));
+    VRT_CUDA(launch(argmax_unkey_kernel, dim3(1), dim3(1), 0, s, false, (const unsigned long long*)ctx->d_key,
+                    reinterpret_cast<uint32_t*>(d_out)));
+    return VRT_OK;
+}
+
+}  // extern "C"

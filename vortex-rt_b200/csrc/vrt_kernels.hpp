@@ -1,0 +1,24 @@
+// Launch entry points shared between runtime.cu and model.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "attention.cuh"
+#include "gemv_q8t.cuh"
+
+namespace vrt {
+
+// Q8T mat-vec with prologue `pro` (Pro) and epilogue `epi` (Epi).
+cudaError_t gemv_q8t(int pro, int epi, const GemvParams& p, int grid, cudaStream_t s, bool pdl);
+uint32_t gemv_smem_bytes(int pro, uint32_t cols);
+cudaError_t gemv_init_attributes();
+cudaError_t argmax_unkey_launch(const unsigned long long* key, uint32_t* out, cudaStream_t s);
+cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl);
+
+// CTAs for a Q8T mat-vec: one per SM, at most one per row group.
+inline int gemv_grid(int sms, uint32_t rows) {
+    const uint32_t groups = (rows + kTileRows - 1) / kTileRows;
+    return static_cast<int>(groups < static_cast<uint32_t>(sms) ? groups : static_cast<uint32_t>(sms));
+}
+
+}  // namespace vrt
