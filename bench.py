@@ -194,6 +194,8 @@ def main():
     ap.add_argument("--workload", default="27b", choices=["27b", "270m"])
     ap.add_argument("--prompt-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
+    ap.add_argument("--vocab", type=int, default=0, help="profiling: smaller vocabulary of the same shape")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -214,6 +216,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     shape = shape_for(args.workload)
+    if args.layers:
+        shape = shape.with_(block_count=args.layers)
+    if args.vocab:
+        shape = shape.with_(vocab_size=args.vocab)
     prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
     e2e_steps = args.steps
     positions = prompt_len + args.warmup + args.steps + e2e_steps + 8

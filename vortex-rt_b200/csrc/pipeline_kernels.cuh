@@ -7,9 +7,13 @@
 // A lane reads each of its blocks with aligned 32-bit loads and realigns
 // the quants with funnel shifts (a block starts 2 bytes off a word boundary
 // in every other position); no read leaves the block's own bytes and the
-// two bytes before it.  The activation vector is quantised once per CTA
-// to int16 per 32-block in shared memory; block sums are exact dp2a integer
-// sums; lanes combine in a fixed shuffle tree, so results replay bit for bit.
+// two bytes before it.  The activation vector is quantised once per CTA,
+// per 32-block, into two int16 digits in shared memory: x ~= s * (hi +
+// lo / 65536), s = amax / 32767, which carries about 31 bits of the block
+// maximum -- as fine as the fp32 input -- so the pipeline entry points meet
+// the reference test programs' absolute tolerances even on large outputs.
+// Block sums are exact dp2a integer sums per digit; lanes combine in a
+// fixed shuffle tree, so results replay bit for bit.
 #pragma once
 
 #include "vrt_device.cuh"
@@ -41,6 +45,7 @@ __global__ void __launch_bounds__(kRawThreads) raw_gemv_kernel(const RawGemvPara
     const uint32_t nblk = p.cols / 32;
     float* sx = reinterpret_cast<float*>(smem);
     int16_t* x16 = reinterpret_cast<int16_t*>(smem + ((nblk * 4 + 15) / 16) * 16);
+    int16_t* x16lo = x16 + p.cols;
     __shared__ unsigned long long warp_best[kRawThreads / 32];
 
     pdl_wait();
@@ -52,17 +57,27 @@ __global__ void __launch_bounds__(kRawThreads) raw_gemv_kernel(const RawGemvPara
             v[e] = p.x[blk * 32 + e];
             amax = fmaxf(amax, fabsf(v[e]));
         }
-        sx[blk] = quant_scale(amax);
+        const float sc = quant_scale(amax);
+        sx[blk] = sc;
         const float inv = amax > 0.0f ? 32767.0f / amax : 0.0f;
+        const float inv_lo = inv * 65536.0f;
 #pragma unroll
         for (int part = 0; part < 4; ++part) {
-            uint32_t wv[4];
+            uint32_t wv[4], wl[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int q0 = quant_one(v[part * 8 + 2 * e], inv), q1 = quant_one(v[part * 8 + 2 * e + 1], inv);
-                wv[e] = (static_cast<uint32_t>(q0) & 0xffffu) | (static_cast<uint32_t>(q1) << 16);
+                int q[2], r[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float xv = v[part * 8 + 2 * e + h];
+                    q[h] = quant_one(xv, inv);
+                    r[h] = quant_one(fmaf(-static_cast<float>(q[h]), sc, xv), inv_lo);
+                }
+                wv[e] = (static_cast<uint32_t>(q[0]) & 0xffffu) | (static_cast<uint32_t>(q[1]) << 16);
+                wl[e] = (static_cast<uint32_t>(r[0]) & 0xffffu) | (static_cast<uint32_t>(r[1]) << 16);
             }
             *reinterpret_cast<uint4*>(x16 + raw_x16_index(blk, part)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            *reinterpret_cast<uint4*>(x16lo + raw_x16_index(blk, part)) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
         }
     }
     __syncthreads();
@@ -105,16 +120,22 @@ __global__ void __launch_bounds__(kRawThreads) raw_gemv_kernel(const RawGemvPara
 #pragma unroll
                     for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(W[i], W[i + 1], 16);
                 }
-                int s = 0;
+                int s = 0, sl = 0;
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
                     const uint4 xv = *reinterpret_cast<const uint4*>(x16 + raw_x16_index(b, part));
+                    const uint4 xl = *reinterpret_cast<const uint4*>(x16lo + raw_x16_index(b, part));
                     s = __dp2a_lo(static_cast<int>(xv.x), static_cast<int>(q[2 * part]), s);
                     s = __dp2a_hi(static_cast<int>(xv.y), static_cast<int>(q[2 * part]), s);
                     s = __dp2a_lo(static_cast<int>(xv.z), static_cast<int>(q[2 * part + 1]), s);
                     s = __dp2a_hi(static_cast<int>(xv.w), static_cast<int>(q[2 * part + 1]), s);
+                    sl = __dp2a_lo(static_cast<int>(xl.x), static_cast<int>(q[2 * part]), sl);
+                    sl = __dp2a_hi(static_cast<int>(xl.y), static_cast<int>(q[2 * part]), sl);
+                    sl = __dp2a_lo(static_cast<int>(xl.z), static_cast<int>(q[2 * part + 1]), sl);
+                    sl = __dp2a_hi(static_cast<int>(xl.w), static_cast<int>(q[2 * part + 1]), sl);
                 }
-                acc += __fmul_rn(half_bits_to_float(scale_bits), sx[b]) * static_cast<float>(s);
+                const float blockv = fmaf(static_cast<float>(sl), 1.0f / 65536.0f, static_cast<float>(s));
+                acc += __fmul_rn(half_bits_to_float(scale_bits), sx[b]) * blockv;
             }
         }
 #pragma unroll

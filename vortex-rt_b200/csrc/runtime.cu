@@ -60,9 +60,23 @@ static cudaError_t gemv_launch_t(const GemvParams& p, int grid, cudaStream_t s, 
     return launch(q8t_gemv_kernel<PRO, EPI>, dim3(grid), dim3(kGemvThreads), smem, s, pdl, p);
 }
 
+// Largest dynamic shared memory a kernel may request: the device's opt-in
+// per-block limit minus the kernel's static shared memory.
+template <typename K>
+static cudaError_t raise_smem_limit(K kernel) {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa{};
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                optin - static_cast<int>(fa.sharedSizeBytes));
+}
+
 template <int PRO, int EPI>
 static cudaError_t gemv_attr_t() {
-    return cudaFuncSetAttribute(q8t_gemv_kernel<PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    return raise_smem_limit(q8t_gemv_kernel<PRO, EPI>);
 }
 
 // Raise the dynamic shared-memory limit of every instantiation once, before
@@ -121,7 +135,7 @@ cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, boo
 
 static int raw_gemv(vrt_ctx* ctx, const RawGemvParams& p, cudaStream_t s) {
     const uint32_t nblk = p.cols / 32;
-    const uint32_t smem = ((nblk * 4 + 15) / 16) * 16 + p.cols * 2;
+    const uint32_t smem = ((nblk * 4 + 15) / 16) * 16 + p.cols * 4;
     const uint32_t rows = p.row_start[p.count];
     const int G = nblk <= 32 ? 8 : (nblk <= 64 ? 16 : 32);
     const uint32_t rows_per_cta = (kRawThreads / 32) * (32 / G);
@@ -132,10 +146,10 @@ static int raw_gemv(vrt_ctx* ctx, const RawGemvParams& p, cudaStream_t s) {
     void (*k)(const RawGemvParams) = G == 8 ? raw_gemv_kernel<8> : (G == 16 ? raw_gemv_kernel<16> : raw_gemv_kernel<32>);
     const int ai = G == 8 ? 0 : (G == 16 ? 1 : 2);
     if (!attr[ai]) {
-        VRT_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        VRT_CUDA(raise_smem_limit(k));
         attr[ai] = true;
     }
-    if (smem > 227u * 1024u) return fail(VRT_E_UNSUPPORTED, "input_dim %u too large for one CTA", p.cols);
+    if (smem > 200u * 1024u) return fail(VRT_E_UNSUPPORTED, "input_dim %u too large for one CTA", p.cols);
     VRT_CUDA(launch(k, dim3(grid), dim3(kRawThreads), smem, s, false, p));
     return VRT_OK;
 }

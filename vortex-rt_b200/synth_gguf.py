@@ -77,7 +77,7 @@ class Gemma3Shape:
 
 # The synthetic configurations named by the benchmark plan.
 SHAPES = {
-    "tiny": Gemma3Shape("tiny", 64, 6, 4, 1, 64, 128, 512, 8, 256),
+    "tiny": Gemma3Shape("tiny", 128, 6, 4, 1, 64, 256, 768, 8, 256),
     "tiny-gqa": Gemma3Shape("tiny-gqa", 128, 6, 8, 2, 64, 256, 768, 8, 256),
     "270m": Gemma3Shape("270m", 640, 18, 4, 1, 256, 2048, 262144, 512, 32768),
     "27b": Gemma3Shape("27b", 5376, 62, 32, 16, 128, 21504, 262144, 1024, 131072),
