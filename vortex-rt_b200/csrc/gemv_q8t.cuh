@@ -49,43 +49,55 @@ struct GemvParams {
     uint32_t zero0_count;
     float* zero1;
     uint32_t zero1_count;
+    uint32_t stage_cap;          // ring slots wanted (0 = as many as fit, up to 8)
 };
 
 constexpr int kConsumerWarps = 8;
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageTiles = kConsumerWarps;
 constexpr int kStageBytes = kStageTiles * kTileBytes;  // 17408
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;
+constexpr uint32_t kSmemBudget = 200u * 1024u;
 constexpr int kChunkGroups = 8;                        // rows reduced per chunk barrier = 128
+constexpr int kPrologueVec = 6;                        // float4 per consumer thread: d <= 6144 in registers
 
 struct GemvSmem {
-    // byte offsets inside dynamic shared memory
-    uint32_t stages, bars, partial, red, sx, x16, xs, total;
+    // byte offsets inside dynamic shared memory; `stages` ring slots at 0
+    uint32_t n_stages, bars, partial, red, sx, x16, xs, total;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(uint32_t cols, int pro) {
+// The weight ring takes whatever the activation buffers leave of a 200 KB
+// budget, up to 8 stages of 17 KB (139 KB in flight per SM).
+__host__ __device__ inline GemvSmem gemv_smem_layout(uint32_t cols, int pro, uint32_t stage_cap = 0) {
     GemvSmem s;
-    s.stages = 0;
-    s.bars = s.stages + kStages * kStageBytes;
-    s.partial = s.bars + 2 * kStages * 8;
-    s.red = s.partial + 2 * kConsumerWarps * kChunkGroups * 16 * 4;
+    const uint32_t partial = 2 * kConsumerWarps * kChunkGroups * 16 * 4;
+    const uint32_t vec = (cols / 32) * 4 + 16 + cols * 2 + 16 + ((pro == kProPlain) ? 0u : cols * 4u);
+    const uint32_t fixed = 2 * kMaxStages * 8 + partial + 64 * 8 + vec;
+    uint32_t ns = (kSmemBudget - fixed) / kStageBytes;
+    const uint32_t cap = stage_cap ? stage_cap : static_cast<uint32_t>(kMaxStages);
+    ns = ns < cap ? ns : cap;
+    s.n_stages = ns > static_cast<uint32_t>(kMaxStages) ? static_cast<uint32_t>(kMaxStages) : (ns < 2 ? 2u : ns);
+    s.bars = s.n_stages * kStageBytes;
+    s.partial = s.bars + 2 * kMaxStages * 8;
+    s.red = s.partial + partial;
     s.sx = s.red + 64 * 8;
     s.x16 = (s.sx + (cols / 32) * 4 + 15) / 16 * 16;
     s.xs = (s.x16 + cols * 2 + 15) / 16 * 16;
-    s.total = s.xs + ((pro == kProPlain || pro == kProRmsInto) ? 0u : cols * 4u);
+    s.total = s.xs + ((pro == kProPlain) ? 0u : cols * 4u);
     return s;
 }
 
-__device__ __forceinline__ int dot16(const uint4 w, const uint4 xl, const uint4 xh, int acc) {
-    acc = __dp2a_lo(static_cast<int>(xl.x), static_cast<int>(w.x), acc);
-    acc = __dp2a_hi(static_cast<int>(xl.y), static_cast<int>(w.x), acc);
-    acc = __dp2a_lo(static_cast<int>(xl.z), static_cast<int>(w.y), acc);
-    acc = __dp2a_hi(static_cast<int>(xl.w), static_cast<int>(w.y), acc);
-    acc = __dp2a_lo(static_cast<int>(xh.x), static_cast<int>(w.z), acc);
-    acc = __dp2a_hi(static_cast<int>(xh.y), static_cast<int>(w.z), acc);
-    acc = __dp2a_lo(static_cast<int>(xh.z), static_cast<int>(w.w), acc);
-    acc = __dp2a_hi(static_cast<int>(xh.w), static_cast<int>(w.w), acc);
-    return acc;
+// 16 int8 weights . 16 int16 activations as two independent dp2a chains.
+__device__ __forceinline__ int dot16(const uint4 w, const uint4 xl, const uint4 xh) {
+    int a = __dp2a_lo(static_cast<int>(xl.x), static_cast<int>(w.x), 0);
+    int b = __dp2a_lo(static_cast<int>(xh.x), static_cast<int>(w.z), 0);
+    a = __dp2a_hi(static_cast<int>(xl.y), static_cast<int>(w.x), a);
+    b = __dp2a_hi(static_cast<int>(xh.y), static_cast<int>(w.z), b);
+    a = __dp2a_lo(static_cast<int>(xl.z), static_cast<int>(w.y), a);
+    b = __dp2a_lo(static_cast<int>(xh.z), static_cast<int>(w.w), b);
+    a = __dp2a_hi(static_cast<int>(xl.w), static_cast<int>(w.y), a);
+    b = __dp2a_hi(static_cast<int>(xh.w), static_cast<int>(w.w), b);
+    return a + b;
 }
 
 // Sum over the 256 consumer threads in fp64, fixed order; result broadcast.
@@ -124,13 +136,95 @@ __device__ __forceinline__ void quant_block(const float* v, uint32_t blk, int16_
     }
 }
 
+// Prologue helper for the norm modes: every consumer thread holds up to
+// kPrologueVec float4 of each input vector in registers, loaded in one round
+// trip; returns x (the activation to quantise) in xs[] (shared, fp32).
+template <int PRO>
+__device__ __forceinline__ void norm_prologue(const GemvParams& p, float* xs, double* red, int ctid) {
+    constexpr int NC = kConsumerWarps * 32;
+    const uint32_t K = p.cols, n4 = K / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(p.x);
+    const float4* h4 = reinterpret_cast<const float4*>(p.h_prev);
+    const float4* wp4 = reinterpret_cast<const float4*>(p.w_post);
+    const float4* wq4 = reinterpret_cast<const float4*>(p.w_pre);
+    float4 a[kPrologueVec], b[kPrologueVec], c[kPrologueVec], w[kPrologueVec];
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < kPrologueVec; ++u) {
+        const uint32_t i = ctid + u * NC;
+        const bool ok = i < n4;
+        a[u] = ok ? x4[i] : z;
+        w[u] = ok ? wq4[i] : z;
+        if (PRO != kProRmsInto) {
+            b[u] = ok ? h4[i] : z;
+            c[u] = ok ? wp4[i] : z;
+        }
+    }
+    auto sq = [](const float4& v) {
+        return static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z +
+               static_cast<double>(v.w) * v.w;
+    };
+    if (PRO != kProRmsInto) {
+        double so = 0.0;
+#pragma unroll
+        for (int u = 0; u < kPrologueVec; ++u) so += sq(a[u]);
+        so = consumer_sum(so, red);
+        const float ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(K)) + p.eps);
+        bool bad = false;
+#pragma unroll
+        for (int u = 0; u < kPrologueVec; ++u) {
+            // rms_norm_inplace(block output, post norm) then += residual
+            float4 h;
+            h.x = __fadd_rn(__fmul_rn(a[u].x, __fmul_rn(ps, c[u].x)), b[u].x);
+            h.y = __fadd_rn(__fmul_rn(a[u].y, __fmul_rn(ps, c[u].y)), b[u].y);
+            h.z = __fadd_rn(__fmul_rn(a[u].z, __fmul_rn(ps, c[u].z)), b[u].z);
+            h.w = __fadd_rn(__fmul_rn(a[u].w, __fmul_rn(ps, c[u].w)), b[u].w);
+            a[u] = h;
+            const uint32_t i = ctid + u * NC;
+            if (i < n4) {
+                bad |= !(isfinite(h.x) && isfinite(h.y) && isfinite(h.z) && isfinite(h.w));
+                if (blockIdx.x == 0) {
+                    if (PRO == kProResid) reinterpret_cast<float4*>(p.h_out)[i] = h;
+                    if (p.trace) reinterpret_cast<float4*>(p.trace)[i] = h;
+                }
+            }
+        }
+        if (bad && blockIdx.x == 0) atomicOr(p.status, kStatusNonFinite);
+    }
+    double ss = 0.0;
+#pragma unroll
+    for (int u = 0; u < kPrologueVec; ++u) ss += sq(a[u]);
+    ss = consumer_sum(ss, red);
+    const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
+#pragma unroll
+    for (int u = 0; u < kPrologueVec; ++u) {
+        const uint32_t i = ctid + u * NC;
+        if (i >= n4) continue;
+        float4 v;
+        if (PRO == kProResidFinal) {  // rms_norm_inplace: x * (scale * w)
+            v.x = __fmul_rn(a[u].x, __fmul_rn(sc, w[u].x));
+            v.y = __fmul_rn(a[u].y, __fmul_rn(sc, w[u].y));
+            v.z = __fmul_rn(a[u].z, __fmul_rn(sc, w[u].z));
+            v.w = __fmul_rn(a[u].w, __fmul_rn(sc, w[u].w));
+            if (blockIdx.x == 0) reinterpret_cast<float4*>(p.h_out)[i] = v;
+        } else {                       // rms_norm_into: (x * scale) * w
+            v.x = __fmul_rn(__fmul_rn(a[u].x, sc), w[u].x);
+            v.y = __fmul_rn(__fmul_rn(a[u].y, sc), w[u].y);
+            v.z = __fmul_rn(__fmul_rn(a[u].z, sc), w[u].z);
+            v.w = __fmul_rn(__fmul_rn(a[u].w, sc), w[u].w);
+        }
+        reinterpret_cast<float4*>(xs)[i] = v;
+    }
+}
+
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const GemvSmem L = gemv_smem_layout(p.cols, PRO);
-    uint8_t* stages = smem + L.stages;
+    const GemvSmem L = gemv_smem_layout(p.cols, PRO, p.stage_cap);
+    const uint32_t NS = L.n_stages;
+    uint8_t* stages = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
-    uint64_t* empty = full + kStages;
+    uint64_t* empty = full + kMaxStages;
     float* partial = reinterpret_cast<float*>(smem + L.partial);
     double* red = reinterpret_cast<double*>(smem + L.red);
     float* sx = reinterpret_cast<float*>(smem + L.sx);
@@ -153,7 +247,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
     const uint32_t n_stages = (n_tiles + kStageTiles - 1) / kStageTiles;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (uint32_t s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
@@ -166,13 +260,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
         // ----------------------------------------------------- producer
         if (lane == 0) {
             const uint8_t* src = p.w + T0 * kTileBytes;
+            uint32_t s = 0, r = 0;
             for (uint32_t st = 0; st < n_stages; ++st) {
-                const uint32_t s = st % kStages, r = st / kStages;
                 if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1)) atomicOr(p.status, kStatusWaitTimeout);
                 const uint32_t tiles = min(static_cast<uint32_t>(kStageTiles), n_tiles - st * kStageTiles);
                 const uint32_t bytes = tiles * kTileBytes;
                 mbar_arrive_expect_tx(&full[s], bytes);
                 bulk_copy_g2s(stages + s * kStageBytes, src + static_cast<uint64_t>(st) * kStageBytes, bytes, &full[s]);
+                if (++s == NS) {
+                    s = 0;
+                    ++r;
+                }
             }
         }
         return;
@@ -196,31 +294,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
 
     const uint32_t K = p.cols, nblk = K / 32;
     if (PRO == kProPlain) {
-        for (uint32_t blk = ctid; blk < nblk; blk += NC) {
-            float v[32];
-            const float4* src = reinterpret_cast<const float4*>(p.x + blk * 32);
+        // blocks of 32 activations: all loads of a thread issued before use
+        for (uint32_t b0 = 0; b0 < nblk; b0 += 3 * NC) {
+            float4 f[3][8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const float4 f = src[q];
-                v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+            for (int q = 0; q < 3; ++q) {
+                const uint32_t blk = b0 + ctid + q * NC;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    f[q][e] = blk < nblk ? reinterpret_cast<const float4*>(p.x + blk * 32)[e]
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
             }
-            quant_block(v, blk, x16p, sx);
-        }
-    } else if (PRO == kProRmsInto) {
-        double ss = 0.0;
-        for (uint32_t k = ctid; k < K; k += NC) ss += static_cast<double>(p.x[k]) * static_cast<double>(p.x[k]);
-        ss = consumer_sum(ss, red);
-        const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
-        for (uint32_t blk = ctid; blk < nblk; blk += NC) {
-            float v[32];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __fmul_rn(__fmul_rn(p.x[blk * 32 + e], scale), p.w_pre[blk * 32 + e]);
-            quant_block(v, blk, x16p, sx);
+            for (int q = 0; q < 3; ++q) {
+                const uint32_t blk = b0 + ctid + q * NC;
+                if (blk < nblk) quant_block(reinterpret_cast<const float*>(f[q]), blk, x16p, sx);
+            }
         }
     } else {
-        // Embed / Resid*: build the new residual in xs[K] first.
-        double ss = 0.0;
         if (PRO == kProEmbed) {
+            double ss = 0.0;
             uint32_t tok = *p.token;
             if (tok >= p.vocab) {
                 if (ctid == 0 && blockIdx.x == 0) atomicOr(p.status, kStatusBadToken);
@@ -236,40 +330,41 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
                 if (blockIdx.x == 0) p.h_out[k] = h;
             }
             ss = consumer_sum(ss, red);
+            const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
+            for (uint32_t k = ctid; k < K; k += NC) xs[k] = __fmul_rn(__fmul_rn(xs[k], scale), p.w_pre[k]);
+        } else if (K <= kPrologueVec * 4 * NC) {
+            norm_prologue<PRO>(p, xs, red, ctid);
         } else {
+            // wide vectors (not used by Gemma 3 shapes): looped form
             double so = 0.0;
-            for (uint32_t k = ctid; k < K; k += NC) so += static_cast<double>(p.x[k]) * static_cast<double>(p.x[k]);
-            so = consumer_sum(so, red);
-            const float post_scale = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(K)) + p.eps);
-            bool bad = false;
+            float ps = 1.0f;
+            if (PRO != kProRmsInto) {
+                for (uint32_t k = ctid; k < K; k += NC) so += static_cast<double>(p.x[k]) * p.x[k];
+                so = consumer_sum(so, red);
+                ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(K)) + p.eps);
+            }
+            double ss = 0.0;
             for (uint32_t k = ctid; k < K; k += NC) {
-                const float n = __fmul_rn(p.x[k], __fmul_rn(post_scale, p.w_post[k]));
-                const float h = __fadd_rn(n, p.h_prev[k]);
+                const float h = PRO == kProRmsInto ? p.x[k]
+                                                   : __fadd_rn(__fmul_rn(p.x[k], __fmul_rn(ps, p.w_post[k])), p.h_prev[k]);
                 xs[k] = h;
-                bad |= !isfinite(h);
-                ss += static_cast<double>(h) * static_cast<double>(h);
-                if (blockIdx.x == 0) {
+                ss += static_cast<double>(h) * h;
+                if (PRO != kProRmsInto && blockIdx.x == 0) {
                     if (PRO == kProResid) p.h_out[k] = h;
                     if (p.trace) p.trace[k] = h;
                 }
             }
-            if (bad && blockIdx.x == 0) atomicOr(p.status, kStatusNonFinite);
             ss = consumer_sum(ss, red);
-        }
-        const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
-        named_bar_sync(1, NC);
-        for (uint32_t blk = ctid; blk < nblk; blk += NC) {
-            float v[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const uint32_t k = blk * 32 + e;
-                // rms_norm_into: (x * scale) * w; rms_norm_inplace: x * (scale * w)
-                v[e] = (PRO == kProResidFinal) ? __fmul_rn(xs[k], __fmul_rn(scale, p.w_pre[k]))
-                                               : __fmul_rn(__fmul_rn(xs[k], scale), p.w_pre[k]);
-                if (PRO == kProResidFinal && blockIdx.x == 0) p.h_out[k] = v[e];
+            const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(K)) + p.eps);
+            for (uint32_t k = ctid; k < K; k += NC) {
+                const float v = PRO == kProResidFinal ? __fmul_rn(xs[k], __fmul_rn(sc, p.w_pre[k]))
+                                                      : __fmul_rn(__fmul_rn(xs[k], sc), p.w_pre[k]);
+                xs[k] = v;
+                if (PRO == kProResidFinal && blockIdx.x == 0) p.h_out[k] = v;
             }
-            quant_block(v, blk, x16p, sx);
         }
+        named_bar_sync(1, NC);
+        for (uint32_t blk = ctid; blk < nblk; blk += NC) quant_block(xs + blk * 32, blk, x16p, sx);
     }
     named_bar_sync(1, NC);
 
@@ -335,31 +430,39 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
         }
     };
 
+    // this warp's tiles are T0 + warp + 8*st; walk (group, column tile) incrementally
+    uint32_t g = static_cast<uint32_t>((T0 + warp) / kt), j = static_cast<uint32_t>((T0 + warp) % kt);
+    uint32_t s = 0, ph = 0;
     for (uint32_t st = 0; st < n_stages; ++st) {
-        const uint32_t s = st % kStages;
-        if (!mbar_wait_bounded(&full[s], (st / kStages) & 1) && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
-        const uint64_t T = T0 + static_cast<uint64_t>(st) * kStageTiles + warp;
-        if (T < T1) {
-            const int g = static_cast<int>(T / kt);
-            const uint32_t j = static_cast<uint32_t>(T % kt);
-            if (g != cur_g && cur_g >= 0) flush(cur_g);
-            const uint32_t c = (static_cast<uint32_t>(g) - g_first) / kChunkGroups;
+        if (!mbar_wait_bounded(&full[s], ph) && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
+        if (T0 + static_cast<uint64_t>(st) * kStageTiles + warp < T1) {
+            if (static_cast<int>(g) != cur_g && cur_g >= 0) flush(cur_g);
+            const uint32_t c = (g - g_first) / kChunkGroups;
             while (chunks_done < c) chunk_end(chunks_done++);
-            cur_g = g;
+            cur_g = static_cast<int>(g);
             const uint8_t* tile = stages + s * kStageBytes + warp * kTileBytes;
             const uint4* tq = reinterpret_cast<const uint4*>(tile);
             const uint4 w0 = tq[lane], w1 = tq[32 + lane], w2 = tq[64 + lane], w3 = tq[96 + lane];
             const uint32_t sc = reinterpret_cast<const uint32_t*>(tile + kTileQBytes)[lane];
             const uint4* xp = reinterpret_cast<const uint4*>(x16p + j * 128);
             const uint4 xa = xp[quad], xb = xp[4 + quad], xc = xp[8 + quad], xd = xp[12 + quad];
-            const int s0 = dot16(w1, xc, xd, dot16(w0, xa, xb, 0));
-            const int s1 = dot16(w3, xc, xd, dot16(w2, xa, xb, 0));
+            const int s0 = dot16(w0, xa, xb) + dot16(w1, xc, xd);
+            const int s1 = dot16(w2, xa, xb) + dot16(w3, xc, xd);
             const float sxb = sx[j * 4 + quad];
             acc0 += __fmul_rn(half_bits_to_float(sc & 0xffffu), sxb) * static_cast<float>(s0);
             acc1 += __fmul_rn(half_bits_to_float(sc >> 16), sxb) * static_cast<float>(s1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+        j += kStageTiles;
+        while (j >= kt) {
+            j -= kt;
+            ++g;
+        }
+        if (++s == NS) {
+            s = 0;
+            ph ^= 1u;
+        }
     }
     if (cur_g >= 0) flush(cur_g);
     while (chunks_done < n_chunks) chunk_end(chunks_done++);

@@ -55,8 +55,17 @@ int check_device_ptr(vrt_ctx* ctx, const void* p, const char* what) {
 // ----------------------------------------------------------- dispatch
 
 template <int PRO, int EPI>
-static cudaError_t gemv_launch_t(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-    const uint32_t smem = gemv_smem_layout(p.cols, PRO).total;
+static cudaError_t gemv_launch_t(const GemvParams& p_in, int grid, cudaStream_t s, bool pdl) {
+    GemvParams p = p_in;
+    if (p.stage_cap == 0) {
+        // ring slots: enough for the largest CTA span, 2..8
+        const uint64_t kt = p.cols / kTileCols;
+        const uint64_t groups = (p.rows + kTileRows - 1) / kTileRows;
+        const uint64_t span = (groups * kt + grid - 1) / grid + kt;
+        const uint64_t st = (span + kStageTiles - 1) / kStageTiles;
+        p.stage_cap = static_cast<uint32_t>(st < 2 ? 2 : (st > kMaxStages ? kMaxStages : st));
+    }
+    const uint32_t smem = gemv_smem_layout(p.cols, PRO, p.stage_cap).total;
     return launch(q8t_gemv_kernel<PRO, EPI>, dim3(grid), dim3(kGemvThreads), smem, s, pdl, p);
 }
 
@@ -115,7 +124,7 @@ cudaError_t gemv_q8t(int pro, int epi, const GemvParams& p, int grid, cudaStream
     return cudaErrorInvalidValue;
 }
 
-uint32_t gemv_smem_bytes(int pro, uint32_t cols) { return gemv_smem_layout(cols, pro).total; }
+uint32_t gemv_smem_bytes(int pro, uint32_t cols) { return gemv_smem_layout(cols, pro, 0).total; }
 
 cudaError_t argmax_unkey_launch(const unsigned long long* key, uint32_t* out, cudaStream_t s) {
     return launch(argmax_unkey_kernel, dim3(1), dim3(1), 0, s, false, key, out);
