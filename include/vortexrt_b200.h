@@ -244,6 +244,18 @@ VRT_API int vrt_model_trace(vrt_model* m, float* h_out);
 VRT_API int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, uint32_t iters,
                                   float* ms_per_launch, uint64_t* algorithmic_bytes);
 
+/* ------------------------------------------------------ tokenizer (host)
+ * The GGUF vocabulary's tokenizer with the reference's rules
+ * (src/gemma3.cpp:289-454 index, 1895-2062 tokenize, 1237-1299 pieces); no
+ * GPU involved. */
+typedef struct vrt_tokenizer vrt_tokenizer;
+VRT_API int vrt_tokenizer_open(const char* gguf_path, vrt_tokenizer** out);
+VRT_API void vrt_tokenizer_close(vrt_tokenizer* t);
+/* Gemma3Model::tokenize: *n receives the id count (ids beyond cap are dropped). */
+VRT_API int vrt_tokenize(vrt_tokenizer* t, const char* text, int add_bos, uint32_t* out, size_t cap, size_t* n);
+/* token_piece (decoded = 0) or decode_piece (decoded = 1), NUL-terminated into out[cap]. */
+VRT_API int vrt_token_piece(vrt_tokenizer* t, uint32_t id, int decoded, char* out, size_t cap, size_t* n);
+
 /* NCCL unique id for tensor parallelism (128 bytes). */
 VRT_API int vrt_tp_unique_id(void* h_out128);
 

@@ -112,6 +112,10 @@ _SIGS = {
     "vrt_model_trace": (_i, [_vp, _vp]),
     "vrt_model_time_kernel": (_i, [_vp, _u32, _u32, _u32, C.POINTER(C.c_float), C.POINTER(_u64)]),
     "vrt_tp_unique_id": (_i, [_vp]),
+    "vrt_tokenizer_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
+    "vrt_tokenizer_close": (None, [_vp]),
+    "vrt_tokenize": (_i, [_vp, C.c_char_p, _i, _vp, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "vrt_token_piece": (_i, [_vp, _u32, _i, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
 }
 
 
@@ -282,6 +286,34 @@ class Model:
         out = np.zeros(c.block_count * c.embedding_length, np.float32)
         check(lib().vrt_model_trace(self.h, _ptr(out)))
         return out.reshape(c.block_count, c.embedding_length)
+
+
+class Tokenizer:
+    """Host tokenizer of a GGUF vocabulary (vrt_tokenizer_*; no GPU)."""
+
+    def __init__(self, path: str):
+        self.h = _vp()
+        check(lib().vrt_tokenizer_open(path.encode(), C.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            lib().vrt_tokenizer_close(self.h)
+            self.h = _vp()
+
+    __del__ = close
+
+    def tokenize(self, text: str, add_bos: bool = True) -> list[int]:
+        data = text.encode()
+        out = np.zeros(4 * len(data) + 8, np.uint32)
+        n = C.c_size_t()
+        check(lib().vrt_tokenize(self.h, data, int(add_bos), _ptr(out), out.size, C.byref(n)))
+        return out[:n.value].tolist()
+
+    def piece(self, token: int, decoded: bool = False) -> bytes:
+        buf = C.create_string_buffer(256)
+        n = C.c_size_t()
+        check(lib().vrt_token_piece(self.h, token, int(decoded), buf, 256, C.byref(n)))
+        return buf.raw[:n.value]
 
 
 def tp_unique_id() -> bytes:
