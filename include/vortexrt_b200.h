@@ -256,6 +256,17 @@ VRT_API int vrt_tokenize(vrt_tokenizer* t, const char* text, int add_bos, uint32
 /* token_piece (decoded = 0) or decode_piece (decoded = 1), NUL-terminated into out[cap]. */
 VRT_API int vrt_token_piece(vrt_tokenizer* t, uint32_t id, int decoded, char* out, size_t cap, size_t* n);
 
+/* ------------------------------------------------- tensor parallelism
+ * Rank `rank` of `world` holds query heads [q_head0, q_head0+q_heads), KV heads
+ * [kv_head0, ...), FFN rows [ffn0, ffn0+ffn) of gate/up (= K columns of down),
+ * and vocab rows [vocab0, vocab0+vocab) of the LM head.  o-proj takes the K
+ * columns of its query heads.  No reference counterpart (the reference is
+ * single-device). */
+typedef struct {
+    uint32_t q_head0, q_heads, kv_head0, kv_heads, ffn0, ffn, vocab0, vocab;
+} vrt_tp_shard;
+VRT_API int vrt_tp_plan(const vrt_gemma3_config* cfg, int world, int rank, vrt_tp_shard* out);
+
 /* NCCL unique id for tensor parallelism (128 bytes). */
 VRT_API int vrt_tp_unique_id(void* h_out128);
 

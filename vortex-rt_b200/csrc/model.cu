@@ -347,21 +347,39 @@ static int validate_config(const vrt_gemma3_config& c) {
     return VRT_OK;
 }
 
-// Shard sizes and the arena plan.
-static int plan(vrt_model* m) {
-    const auto& c = m->cfg;
-    const int W = m->world;
+// Tensor-parallel shard of one rank: heads, FFN rows and vocab rows split in
+// equal contiguous ranges; every piece keeps whole 128-column tiles.
+static int tp_plan(const vrt_gemma3_config& c, int W, int rank, vrt_tp_shard& s) {
+    if (W < 1 || rank < 0 || rank >= W) return fail(VRT_E_INVALID, "bad tensor-parallel rank %d of %d", rank, W);
     if (c.head_count_kv % W || c.head_count % W || c.feed_forward_length % (W * 128) || c.vocab_size % (W * 16)) {
         return fail(VRT_E_UNSUPPORTED, "model does not split evenly over %d ranks", W);
     }
-    m->Hl = c.head_count / W;
-    m->KVl = c.head_count_kv / W;
+    if ((c.head_count / W) * c.head_dim % 128) {
+        return fail(VRT_E_UNSUPPORTED, "per-rank attention width must be a multiple of 128");
+    }
+    s.q_heads = c.head_count / W;
+    s.q_head0 = s.q_heads * rank;
+    s.kv_heads = c.head_count_kv / W;
+    s.kv_head0 = s.kv_heads * rank;
+    s.ffn = c.feed_forward_length / W;
+    s.ffn0 = s.ffn * rank;
+    s.vocab = c.vocab_size / W;
+    s.vocab0 = s.vocab * rank;
+    return VRT_OK;
+}
+
+// Shard sizes and the arena plan.
+static int plan(vrt_model* m) {
+    const auto& c = m->cfg;
+    vrt_tp_shard sh{};
+    VRT_TRY(tp_plan(c, m->world, m->rank, sh));
+    m->Hl = sh.q_heads;
+    m->KVl = sh.kv_heads;
     m->qwl = m->Hl * c.head_dim;
     m->kwl = m->KVl * c.head_dim;
-    m->ffl = c.feed_forward_length / W;
-    if (m->qwl % 128) return fail(VRT_E_UNSUPPORTED, "per-rank attention width must be a multiple of 128");
-    m->vocab_lo = c.vocab_size / W * m->rank;
-    m->vocab_hi = c.vocab_size / W * (m->rank + 1);
+    m->ffl = sh.ffn;
+    m->vocab_lo = sh.vocab0;
+    m->vocab_hi = sh.vocab0 + sh.vocab;
     const uint32_t d = c.embedding_length;
     uint64_t at = 0;
     m->embd = at;
@@ -1411,6 +1429,13 @@ int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, uint32_t
     cudaEventDestroy(e1);
     *ms_per_launch = ms / static_cast<float>(iters);
     return VRT_OK;
+}
+
+int vrt_tp_plan(const vrt_gemma3_config* cfg, int world, int rank, vrt_tp_shard* out) {
+    clear_error();
+    if (!cfg || !out) return fail(VRT_E_INVALID, "null argument");
+    VRT_TRY(validate_config(*cfg));
+    return tp_plan(*cfg, world, rank, *out);
 }
 
 int vrt_tp_unique_id(void* h_out128) {

@@ -57,6 +57,11 @@ class DeviceInfo(C.Structure):
                 ("l2_bytes", C.c_uint64)]
 
 
+class TpShard(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("q_head0", "q_heads", "kv_head0", "kv_heads", "ffn0", "ffn", "vocab0",
+                                          "vocab")]
+
+
 class ArgmaxResult(C.Structure):
     _fields_ = [("index", C.c_uint32), ("value", C.c_float)]
 
@@ -112,6 +117,7 @@ _SIGS = {
     "vrt_model_trace": (_i, [_vp, _vp]),
     "vrt_model_time_kernel": (_i, [_vp, _u32, _u32, _u32, C.POINTER(C.c_float), C.POINTER(_u64)]),
     "vrt_tp_unique_id": (_i, [_vp]),
+    "vrt_tp_plan": (_i, [C.POINTER(Gemma3Config), _i, _i, C.POINTER(TpShard)]),
     "vrt_tokenizer_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
     "vrt_tokenizer_close": (None, [_vp]),
     "vrt_tokenize": (_i, [_vp, C.c_char_p, _i, _vp, C.c_size_t, C.POINTER(C.c_size_t)]),
@@ -314,6 +320,12 @@ class Tokenizer:
         n = C.c_size_t()
         check(lib().vrt_token_piece(self.h, token, int(decoded), buf, 256, C.byref(n)))
         return buf.raw[:n.value]
+
+
+def tp_plan(config: Gemma3Config, world: int, rank: int) -> TpShard:
+    s = TpShard()
+    check(lib().vrt_tp_plan(C.byref(config), world, rank, C.byref(s)))
+    return s
 
 
 def tp_unique_id() -> bytes:
