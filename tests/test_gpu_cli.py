@@ -18,7 +18,7 @@ CLI = os.path.join(os.path.dirname(vrt.LIB_PATH), "vortexrt-gemma")
 
 
 def run(*args):
-    p = subprocess.run([CLI, *args], capture_output=True, text=True, timeout=600)
+    p = subprocess.run([CLI, *args], capture_output=True, text=True, errors="replace", timeout=600)
     assert p.returncode == 0, p.stderr
     assert "Validation: OK" in p.stdout
     return p.stdout

@@ -66,10 +66,36 @@ __device__ __forceinline__ void head_norm_rope(float (&v)[M], const float* w, co
     }
 }
 
+// Positions a warp loads at once: all their K/V loads are in flight together.
+template <int M>
+struct AttnBatch {
+    static constexpr int P = M >= 8 ? 4 : 8;
+};
+
+// K/V of positions tb + i*4 (i < P) of one KV head; positions outside
+// [.., t1) and the newest position `pos` (not yet in the cache) read as 0.
+template <int M, int P>
+__device__ __forceinline__ void load_kv_batch(float (&kb)[P][M], float (&vb)[P][M], const float* kc,
+                                              const float* vc, uint32_t tb, uint32_t t1, uint32_t pos,
+                                              uint32_t cap, uint32_t hd, int lane) {
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+        const uint32_t t = tb + i * kAttnWarps;
+        const bool ok = t < t1 && t != pos;
+        const uint64_t base = static_cast<uint64_t>(ok ? t % cap : 0u) * hd + lane;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            kb[i][m] = ok ? __ldcg(kc + base + 32 * m) : 0.0f;
+            vb[i][m] = ok ? __ldcg(vc + base + 32 * m) : 0.0f;
+        }
+    }
+}
+
 // M = head_dim / 32, RG >= H / KV (1, 2, 4 or 8).
 template <int M, int RG>
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
     constexpr int HD = M * 32;
+    constexpr int P = AttnBatch<M>::P;
     __shared__ float q_s[RG][HD];
     __shared__ float knew[HD], vnew[HD];
     __shared__ float w_ml[kAttnWarps][RG][2];
@@ -77,22 +103,33 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     __shared__ uint32_t last_flag;
 
     pdl_trigger();
-    pdl_wait();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t g = blockIdx.y, s = blockIdx.x;
     const uint32_t R = p.H / p.KV, hd = p.hd;
-    if (p.zero0) {
-        const uint32_t nb = gridDim.x * gridDim.y, b = blockIdx.y * gridDim.x + blockIdx.x;
-        const uint32_t a0 = static_cast<uint64_t>(p.zero0_count) * b / nb;
-        const uint32_t a1 = static_cast<uint64_t>(p.zero0_count) * (b + 1) / nb;
-        for (uint32_t i = a0 + tid; i < a1; i += kAttnThreads) p.zero0[i] = 0.0f;
-    }
+
+    // Nothing the step chain writes is read before griddepcontrol.wait --
+    // not even the position: under programmatic launch the previous step's
+    // finalize may still be in flight when this grid starts.
+    pdl_wait();
     const uint32_t pos = *p.pos;
     const uint32_t n = p.window ? min(pos + 1, p.window) : pos + 1;
     const uint32_t first = pos + 1 - n;  // oldest position attended
     const uint32_t chunk = (n + p.splits - 1) / p.splits;
     const uint32_t t0 = first + s * chunk;
     const uint32_t t1 = min(first + n, t0 + chunk);
+    const float* kc = p.k_cache + static_cast<uint64_t>(g) * p.cap * hd;
+    const float* vc = p.v_cache + static_cast<uint64_t>(g) * p.cap * hd;
+
+    // the first batch of older positions is in flight during the query prologue
+    float kb[P][M], vb[P][M];
+    load_kv_batch<M, P>(kb, vb, kc, vc, t0 + warp, t1, pos, p.cap, hd, lane);
+
+    if (p.zero0) {
+        const uint32_t nb = gridDim.x * gridDim.y, b = blockIdx.y * gridDim.x + blockIdx.x;
+        const uint32_t a0 = static_cast<uint64_t>(p.zero0_count) * b / nb;
+        const uint32_t a1 = static_cast<uint64_t>(p.zero0_count) * (b + 1) / nb;
+        for (uint32_t i = a0 + tid; i < a1; i += kAttnThreads) p.zero0[i] = 0.0f;
+    }
     const float* cs = p.rope_cos + static_cast<uint64_t>(pos) * (hd / 2);
     const float* sn = p.rope_sin + static_cast<uint64_t>(pos) * (hd / 2);
 
@@ -129,7 +166,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     }
     __syncthreads();
 
-    // 3. online softmax over this CTA's positions
+    // 3. online softmax, P positions per warp step
     float mx[RG], sm[RG], acc[RG][M];
 #pragma unroll
     for (int r = 0; r < RG; ++r) {
@@ -138,36 +175,55 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
 #pragma unroll
         for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
     }
-    for (uint32_t t = t0 + warp; t < t1; t += kAttnWarps) {
-        float kv[M], vv[M];
-        if (t == pos) {
+    for (uint32_t tb = t0 + warp; tb < t1; tb += P * kAttnWarps) {
+        // the newest position (only ever inside this CTA's range) comes from shared memory
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+            if (has_new && tb + i * kAttnWarps == pos) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    kb[i][m] = knew[lane + 32 * m];
+                    vb[i][m] = vnew[lane + 32 * m];
+                }
+            }
+        }
+        float kcur[P][M], vcur[P][M];
+#pragma unroll
+        for (int i = 0; i < P; ++i)
 #pragma unroll
             for (int m = 0; m < M; ++m) {
-                kv[m] = knew[lane + 32 * m];
-                vv[m] = vnew[lane + 32 * m];
+                kcur[i][m] = kb[i][m];
+                vcur[i][m] = vb[i][m];
             }
-        } else {
-            const uint64_t base = (static_cast<uint64_t>(g) * p.cap + (t % p.cap)) * hd;
-#pragma unroll
-            for (int m = 0; m < M; ++m) {
-                kv[m] = __ldcg(p.k_cache + base + lane + 32 * m);
-                vv[m] = __ldcg(p.v_cache + base + lane + 32 * m);
-            }
+        if (tb + P * kAttnWarps < t1) {  // next batch in flight
+            load_kv_batch<M, P>(kb, vb, kc, vc, tb + P * kAttnWarps, t1, pos, p.cap, hd, lane);
         }
 #pragma unroll
         for (int r = 0; r < RG; ++r) {
             if (r < static_cast<int>(R)) {
-                float d = 0.0f;
+                float sc[P];
+                float bm = -INFINITY;
 #pragma unroll
-                for (int m = 0; m < M; ++m) d = fmaf(q_s[r][lane + 32 * m], kv[m], d);
-                d = warp_sum(d);
-                const float sc = d * p.scale;
-                const float nm = fmaxf(mx[r], sc);
+                for (int i = 0; i < P; ++i) {
+                    float d = 0.0f;
+#pragma unroll
+                    for (int m = 0; m < M; ++m) d = fmaf(q_s[r][lane + 32 * m], kcur[i][m], d);
+                    d = warp_sum(d);
+                    sc[i] = (tb + i * kAttnWarps < t1) ? d * p.scale : -INFINITY;
+                    bm = fmaxf(bm, sc[i]);
+                }
+                const float nm = fmaxf(mx[r], bm);
                 const float corr = expf(mx[r] - nm);
-                const float pr = expf(sc - nm);
-                sm[r] = sm[r] * corr + pr;
+                sm[r] *= corr;
 #pragma unroll
-                for (int m = 0; m < M; ++m) acc[r][m] = fmaf(pr, vv[m], acc[r][m] * corr);
+                for (int m = 0; m < M; ++m) acc[r][m] *= corr;
+#pragma unroll
+                for (int i = 0; i < P; ++i) {
+                    const float pr = expf(sc[i] - nm);
+                    sm[r] += pr;
+#pragma unroll
+                    for (int m = 0; m < M; ++m) acc[r][m] = fmaf(pr, vcur[i][m], acc[r][m]);
+                }
                 mx[r] = nm;
             }
         }
@@ -216,16 +272,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    // 4. merge splits in order
+    // 4. merge the splits that saw positions, in split order
+    const uint32_t used = min(p.splits, (n + chunk - 1) / chunk);
     for (uint32_t r = warp; r < R; r += kAttnWarps) {
         const uint32_t h = g * R + r;
         const float* ml = p.part_ml + static_cast<uint64_t>(h) * p.splits * 2;
         float M_ = -INFINITY;
-        for (uint32_t q = 0; q < p.splits; ++q) M_ = fmaxf(M_, __ldcg(ml + 2 * q));
+        for (uint32_t q = 0; q < used; ++q) M_ = fmaxf(M_, __ldcg(ml + 2 * q));
         float L_ = 0.0f, a[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) a[m] = 0.0f;
-        for (uint32_t q = 0; q < p.splits; ++q) {
+        for (uint32_t q = 0; q < used; ++q) {
             const float mq = __ldcg(ml + 2 * q);
             if (mq == -INFINITY) continue;
             const float f = expf(mq - M_);

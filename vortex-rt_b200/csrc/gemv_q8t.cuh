@@ -50,7 +50,32 @@ struct GemvParams {
     float* zero1;
     uint32_t zero1_count;
     uint32_t stage_cap;          // ring slots wanted (0 = as many as fit, up to 8)
+    // L2 prefetch of the next mat-vec of the step: after issuing its own
+    // copies, CTA b prefetches the first pf_bytes of CTA b's span in the
+    // next kernel (same partition rule, next_group: group-granular spans).
+    const uint8_t* next_w;
+    uint32_t next_rows, next_cols, next_grid, next_group, pf_bytes;
 };
+
+// First tile of CTA b's span under the partition rule of the kernel below.
+__host__ __device__ inline uint64_t gemv_span_start(uint32_t rows, uint32_t cols, uint32_t grid, uint32_t b,
+                                                    bool group_granular) {
+    const uint64_t kt = cols / kTileCols, groups = (rows + kTileRows - 1) / kTileRows;
+    return group_granular ? groups * b / grid * kt : groups * kt * b / grid;
+}
+
+__device__ __forceinline__ void prefetch_next_span(const GemvParams& p) {
+    if (!p.next_w || blockIdx.x >= p.next_grid) return;
+    const uint64_t t0 = gemv_span_start(p.next_rows, p.next_cols, p.next_grid, blockIdx.x, p.next_group != 0);
+    const uint64_t t1 = gemv_span_start(p.next_rows, p.next_cols, p.next_grid, blockIdx.x + 1, p.next_group != 0);
+    uint64_t bytes = (t1 - t0) * kTileBytes;
+    if (bytes > p.pf_bytes) bytes = p.pf_bytes;
+    const uint8_t* src = p.next_w + t0 * kTileBytes;
+    for (uint64_t off = 0; off < bytes; off += 32768) {
+        const uint64_t n = bytes - off < 32768 ? bytes - off : 32768;
+        bulk_prefetch_l2(src + off, static_cast<uint32_t>(n));
+    }
+}
 
 constexpr int kConsumerWarps = 8;
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
@@ -260,18 +285,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
         // ----------------------------------------------------- producer
         if (lane == 0) {
             const uint8_t* src = p.w + T0 * kTileBytes;
+            const uint64_t pol = l2_policy_evict_first();
             uint32_t s = 0, r = 0;
             for (uint32_t st = 0; st < n_stages; ++st) {
                 if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1)) atomicOr(p.status, kStatusWaitTimeout);
                 const uint32_t tiles = min(static_cast<uint32_t>(kStageTiles), n_tiles - st * kStageTiles);
                 const uint32_t bytes = tiles * kTileBytes;
                 mbar_arrive_expect_tx(&full[s], bytes);
-                bulk_copy_g2s(stages + s * kStageBytes, src + static_cast<uint64_t>(st) * kStageBytes, bytes, &full[s]);
+                bulk_copy_g2s_hint(stages + s * kStageBytes, src + static_cast<uint64_t>(st) * kStageBytes, bytes,
+                                   &full[s], pol);
                 if (++s == NS) {
                     s = 0;
                     ++r;
                 }
             }
+            prefetch_next_span(p);
         }
         return;
     }

@@ -706,6 +706,33 @@ static int nccl_sum(vrt_model* m, float* buf, size_t n, cudaStream_t s) {
     return VRT_OK;
 }
 
+// The mat-vecs of one decode step, in launch order: weight base, rows, cols,
+// and whether the epilogue partitions by whole row groups.
+struct StepGemv {
+    const uint8_t* w;
+    uint32_t rows, cols;
+    bool group;
+};
+
+static std::vector<StepGemv> step_gemvs(vrt_model* m, bool head) {
+    const auto& c = m->cfg;
+    const uint32_t d = c.embedding_length;
+    std::vector<StepGemv> v;
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const auto& L = m->layers[l];
+        v.push_back({m->arena + L.qkv, m->qwl + 2 * m->kwl, d, false});
+        v.push_back({m->arena + L.o, d, m->qwl, false});
+        v.push_back({m->arena + L.gu, 2 * m->ffl, d, true});
+        v.push_back({m->arena + L.down, d, m->ffl, false});
+    }
+    if (head) {
+        const uint32_t kt = d / kTileCols;
+        v.push_back({m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes,
+                     m->vocab_hi - m->vocab_lo, d, true});
+    }
+    return v;
+}
+
 static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernels) {
     const auto& c = m->cfg;
     const bool pdl = m->opt.use_pdl != 0;
@@ -715,9 +742,21 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
     uint32_t* status = &m->st->status;
     float* trace = m->trace_on ? m->trace : nullptr;
     auto F = [&](uint64_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+    // next-kernel L2 prefetch chain; the step's last mat-vec points at the
+    // first one (the next step starts with it)
+    const std::vector<StepGemv> seq = step_gemvs(m, head);
+    size_t gi = 0;
     auto gemv = [&](int pro, int epi, GemvParams p) -> int {
         p.status = status;
         p.eps = c.rms_epsilon;
+        const StepGemv& nx = seq[(gi + 1) % seq.size()];
+        p.next_w = nx.w;
+        p.next_rows = nx.rows;
+        p.next_cols = nx.cols;
+        p.next_grid = static_cast<uint32_t>(gemv_grid(sms, nx.rows));
+        p.next_group = nx.group ? 1u : 0u;
+        p.pf_bytes = 64u * 1024u;
+        ++gi;
         VRT_CUDA(gemv_q8t(pro, epi, p, gemv_grid(sms, p.rows), s, pdl));
         ++nk;
         return VRT_OK;
