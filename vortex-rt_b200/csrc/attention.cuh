@@ -22,6 +22,8 @@ namespace vrt {
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 8;   // query heads per KV head handled by one CTA
+// History splits per KV head are capped at kAttnWarps * head_dim (the merge
+// keeps one weight per split in the warp-merge buffer).
 
 struct AttnParams {
     const float* qkv;       // q [H*hd] | k [KV*hd] | v [KV*hd]
@@ -272,24 +274,46 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    // 4. merge the splits that saw positions, in split order
+    // 4. merge the splits that saw positions, in split order: split maxima
+    //    and weights one split per lane, then the accumulators with eight
+    //    splits' loads in flight per lane
     const uint32_t used = min(p.splits, (n + chunk - 1) / chunk);
     for (uint32_t r = warp; r < R; r += kAttnWarps) {
         const uint32_t h = g * R + r;
         const float* ml = p.part_ml + static_cast<uint64_t>(h) * p.splits * 2;
+        const float* pa = p.part_acc + static_cast<uint64_t>(h) * p.splits * hd;
+        // split weights reuse the warp-merge buffer (free once this CTA's partial is out)
+        float* fw = &w_acc[0][0][0] + r * (kAttnWarps * HD);
         float M_ = -INFINITY;
-        for (uint32_t q = 0; q < used; ++q) M_ = fmaxf(M_, __ldcg(ml + 2 * q));
-        float L_ = 0.0f, a[M];
+        for (uint32_t q = lane; q < used; q += 32) M_ = fmaxf(M_, __ldcg(ml + 2 * q));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, o));
+        float L_ = 0.0f;
+        for (uint32_t q = lane; q < used; q += 32) {
+            const float mq = __ldcg(ml + 2 * q);
+            const float f = mq == -INFINITY ? 0.0f : expf(mq - M_);
+            fw[q] = f;
+            L_ += __ldcg(ml + 2 * q + 1) * f;
+        }
+        L_ = warp_sum(L_);
+        __syncwarp();
+        float a[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) a[m] = 0.0f;
-        for (uint32_t q = 0; q < used; ++q) {
-            const float mq = __ldcg(ml + 2 * q);
-            if (mq == -INFINITY) continue;
-            const float f = expf(mq - M_);
-            L_ += __ldcg(ml + 2 * q + 1) * f;
-            const float* pa = p.part_acc + (static_cast<uint64_t>(h) * p.splits + q) * hd;
+        for (uint32_t q0 = 0; q0 < used; q0 += 8) {
+            float v[8][M];
 #pragma unroll
-            for (int m = 0; m < M; ++m) a[m] = fmaf(__ldcg(pa + lane + 32 * m), f, a[m]);
+            for (int u = 0; u < 8; ++u) {
+                const uint32_t q = q0 + u;
+#pragma unroll
+                for (int m = 0; m < M; ++m) v[u][m] = q < used ? __ldcg(pa + q * hd + lane + 32 * m) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float f = q0 + u < used ? fw[q0 + u] : 0.0f;
+#pragma unroll
+                for (int m = 0; m < M; ++m) a[m] = fmaf(v[u][m], f, a[m]);
+            }
         }
         const float inv = 1.0f / L_;
 #pragma unroll

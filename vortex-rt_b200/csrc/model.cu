@@ -453,8 +453,8 @@ static int alloc_runtime(vrt_model* m) {
         L.cap = (!L.global && c.sliding_window) ? std::min(c.sliding_window, P) : P;
         kv_floats += 2ull * m->KVl * L.cap * hd;
         const uint32_t by_len = std::max(1u, (L.cap + 15) / 16);
-        const uint32_t by_sm = std::max(1u, static_cast<uint32_t>(2 * sms) / m->KVl);
-        L.splits = std::min(by_len, by_sm);
+        const uint32_t by_sm = std::max(1u, static_cast<uint32_t>(3 * sms) / m->KVl);
+        L.splits = std::min(std::min(by_len, by_sm), static_cast<uint32_t>(kAttnWarps) * hd);
         max_splits = std::max(max_splits, L.splits);
     }
     VRT_CUDA(cudaMalloc(&m->kv_mem, kv_floats * 4));
