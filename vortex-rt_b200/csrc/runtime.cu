@@ -142,25 +142,37 @@ cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, boo
     return cudaErrorInvalidValue;
 }
 
-static int raw_gemv(vrt_ctx* ctx, const RawGemvParams& p, cudaStream_t s) {
+static int raw_gemv_sms(int sms, const RawGemvParams& p, cudaStream_t s) {
     const uint32_t nblk = p.cols / 32;
     const uint32_t smem = ((nblk * 4 + 15) / 16) * 16 + p.cols * 4;
     const uint32_t rows = p.row_start[p.count];
     const int G = nblk <= 32 ? 8 : (nblk <= 64 ? 16 : 32);
     const uint32_t rows_per_cta = (kRawThreads / 32) * (32 / G);
     int occ = 2;
-    const uint32_t max_grid = static_cast<uint32_t>(ctx->prop.multiProcessorCount) * occ;
+    const uint32_t max_grid = static_cast<uint32_t>(sms) * occ;
     const uint32_t grid = std::max(1u, std::min(max_grid, (rows + rows_per_cta - 1) / rows_per_cta));
-    static bool attr[3] = {false, false, false};
+    // the shared-memory limit is a per-device function attribute
+    static std::mutex mu;
+    static uint64_t attr_done[3] = {0, 0, 0};  // bit d: set on device d
     void (*k)(const RawGemvParams) = G == 8 ? raw_gemv_kernel<8> : (G == 16 ? raw_gemv_kernel<16> : raw_gemv_kernel<32>);
     const int ai = G == 8 ? 0 : (G == 16 ? 1 : 2);
-    if (!attr[ai]) {
-        VRT_CUDA(raise_smem_limit(k));
-        attr[ai] = true;
+    int dev = 0;
+    VRT_CUDA(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> g(mu);
+        const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+        if (!(attr_done[ai] & bit)) {
+            VRT_CUDA(raise_smem_limit(k));
+            attr_done[ai] |= bit;
+        }
     }
     if (smem > 200u * 1024u) return fail(VRT_E_UNSUPPORTED, "input_dim %u too large for one CTA", p.cols);
     VRT_CUDA(launch(k, dim3(grid), dim3(kRawThreads), smem, s, false, p));
     return VRT_OK;
+}
+
+static int raw_gemv(vrt_ctx* ctx, const RawGemvParams& p, cudaStream_t s) {
+    return raw_gemv_sms(ctx->prop.multiProcessorCount, p, s);
 }
 
 static int check_q8_matrix(uint64_t weights_bytes, uint64_t off, uint32_t in, uint32_t out, const char* what) {
