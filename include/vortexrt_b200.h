@@ -114,6 +114,20 @@ VRT_API int vrt_q8_ffn(vrt_ctx* ctx, const void* d_weights, uint64_t weights_byt
                        float* d_workspace, float* d_y, uint32_t input_dim, uint32_t ffn_dim,
                        uint32_t output_dim, void* stream);
 
+/* The fused FFN above for callers that cannot allocate device memory: no
+ * context and no workspace argument; runs on the current device.  No
+ * counterpart in the reference.  The gate/up intermediate lives in a
+ * library-owned device array of 2 * 32768 floats (256 KB on every GPU that
+ * loads the library, held until exit), so ffn_dim <= 32768 (larger sizes
+ * return VRT_E_INVALID) and nothing is ever allocated.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams, other threads) race on it.
+ * `stream` NULL = the CUDA default stream. */
+VRT_API int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t gate_off,
+                              uint64_t up_off, uint64_t down_off, const float* d_x, float* d_y,
+                              uint32_t input_dim, uint32_t ffn_dim, uint32_t output_dim, void* stream);
+
 /* gate[i] = gelu_tanh(gate[i]) * up[i].  Replaces shaders/gelu_mul.comp. */
 VRT_API int vrt_gelu_mul(vrt_ctx* ctx, float* d_gate, const float* d_up, uint32_t count, void* stream);
 

@@ -397,6 +397,96 @@ int vrt_q8_ffn(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes, uint
     return vrt_q8_gemv(ctx, d_weights, weights_bytes, down_off, d_ws, d_y, ffn_dim, output_dim, stream);
 }
 
+// ------------------------------------------------------------------------
+// Fused FFN for callers that cannot allocate device memory.
+//
+// vrt_q8_ffn needs a context (whose creation allocates) and a caller-owned
+// workspace for the gate and up projections.  Some callers cannot do either:
+// code that runs where device allocation is forbidden or unavailable -- inside
+// another framework's memory pool that must not grow, in an embedded host
+// that has pre-reserved all device memory, or in a tool that may only launch
+// work.  For them the gate/up intermediate lives in this file-scope device
+// array, which every GPU that loads the library holds until the process exits.
+constexpr uint32_t kStaticFfnMax = 32768;  // largest ffn_dim accepted
+static __device__ __align__(256) float g_ffn_scratch[2 * kStaticFfnMax];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+float* g_static_ptr[kMaxDevices] = {};
+int g_static_sms[kMaxDevices] = {};
+}  // namespace
+
+}  // extern "C": reopened after the set-up helper
+
+// Device address of g_ffn_scratch on the current device.  In host code the
+// array's name only stands in for the device symbol, so the address must come
+// from cudaGetSymbolAddress, once per device, with that device current.
+static int static_ffn_setup(float** ptr, int* sms) {
+    int dev = 0;
+    VRT_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(VRT_E_UNSUPPORTED, "device %d beyond %d", dev, kMaxDevices);
+    std::lock_guard<std::mutex> g(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        VRT_CUDA(cudaGetSymbolAddress(&p, g_ffn_scratch));
+        int n = 0;
+        VRT_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        g_static_ptr[dev] = static_cast<float*>(p);
+        g_static_sms[dev] = n;
+    }
+    *ptr = g_static_ptr[dev];
+    *sms = g_static_sms[dev];
+    return VRT_OK;
+}
+
+extern "C" {
+
+int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t gate_off, uint64_t up_off,
+                      uint64_t down_off, const float* d_x, float* d_y, uint32_t input_dim, uint32_t ffn_dim,
+                      uint32_t output_dim, void* stream) {
+    clear_error();
+    if (!d_weights || !d_x || !d_y) return fail(VRT_E_INVALID, "Q8 fused FFN: null argument");
+    if (!input_dim || !ffn_dim || !output_dim || input_dim % 32 || ffn_dim % 32) {
+        return fail(VRT_E_INVALID, "Q8 fused FFN dimensions must be non-zero and Q8 aligned");
+    }
+    if (ffn_dim > kStaticFfnMax) {
+        return fail(VRT_E_INVALID, "vrt_q8_ffn_static: ffn_dim %u exceeds the static scratch limit of %u", ffn_dim,
+                    kStaticFfnMax);
+    }
+    VRT_TRY(check_q8_matrix(weights_bytes, gate_off, input_dim, ffn_dim, "Q8 fused FFN gate"));
+    VRT_TRY(check_q8_matrix(weights_bytes, up_off, input_dim, ffn_dim, "Q8 fused FFN up"));
+    VRT_TRY(check_q8_matrix(weights_bytes, down_off, ffn_dim, output_dim, "Q8 fused FFN down"));
+    float* ws = nullptr;
+    int sms = 0;
+    VRT_TRY(static_ffn_setup(&ws, &sms));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // gate and up are written in full before gelu_mul reads them: the scratch
+    // needs no clearing between calls
+    RawGemvParams p{};
+    p.w = static_cast<const uint8_t*>(d_weights);
+    p.offsets[0] = gate_off;
+    p.offsets[1] = up_off;
+    p.row_start[1] = ffn_dim;
+    p.row_start[2] = 2 * ffn_dim;
+    p.count = 2;
+    p.cols = input_dim;
+    p.x = d_x;
+    p.y = ws;
+    VRT_TRY(raw_gemv_sms(sms, p, s));
+    VRT_CUDA(launch(gelu_mul_kernel, dim3((ffn_dim + 255) / 256), dim3(256), 0, s, false, ws, (const float*)(ws + ffn_dim),
+                    ffn_dim));
+    RawGemvParams d{};
+    d.w = static_cast<const uint8_t*>(d_weights);
+    d.offsets[0] = down_off;
+    d.row_start[1] = output_dim;
+    d.count = 1;
+    d.cols = ffn_dim;
+    d.x = ws;
+    d.y = d_y;
+    return raw_gemv_sms(sms, d, s);
+}
+
 int vrt_argmax(vrt_ctx* ctx, const float* d_x, uint32_t count, vrt_argmax_result* d_out, void* stream) {
     clear_error();
     if (!ctx || !d_x || !d_out) return fail(VRT_E_INVALID, "ArgmaxPipeline: null argument");

@@ -88,6 +88,7 @@ _SIGS = {
     "vrt_q8_gemv": (_i, [_vp, _vp, _u64, _u64, _vp, _vp, _u32, _u32, _vp]),
     "vrt_q8_gemv_multi": (_i, [_vp, _vp, _u64, _vp, _vp, _u32, _vp, _vp, _u32, _vp]),
     "vrt_q8_ffn": (_i, [_vp, _vp, _u64, _u64, _u64, _u64, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "vrt_q8_ffn_static": (_i, [_vp, _u64, _u64, _u64, _u64, _vp, _vp, _u32, _u32, _u32, _vp]),
     "vrt_gelu_mul": (_i, [_vp, _vp, _vp, _u32, _vp]),
     "vrt_argmax": (_i, [_vp, _vp, _u32, _vp, _vp]),
     "vrt_lm_head_argmax": (_i, [_vp, _vp, _u64, _u64, _vp, _u32, _u32, _vp, _vp, _vp]),
