@@ -196,6 +196,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
     ap.add_argument("--vocab", type=int, default=0, help="profiling: smaller vocabulary of the same shape")
+    ap.add_argument("--tp-exchange", default="peer", choices=["peer", "nccl"],
+                    help="tensor parallelism: peer-memory exchange fused into the consumer kernels, or NCCL all-reduce")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -233,7 +235,7 @@ def main():
     ctx = vrt.Context(local)
     cfg = vrt.Gemma3Config.from_shape(shape)
     m = vrt.Model(ctx, None, config=cfg, seed=1234, max_positions=positions, tp_rank=rank, tp_world=world,
-                  nccl_id=nccl_id)
+                  nccl_id=nccl_id, tp_exchange=args.tp_exchange)
     kernels = m.step_kernels()
 
     def barrier():
@@ -310,6 +312,8 @@ def main():
                        "ffn": shape.feed_forward_length, "vocab": shape.vocab_size, "global_batch": 1,
                        "positions": f"{prompt_len + args.warmup}..{prompt_len + args.warmup + args.steps}",
                        "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                       "tp_exchange": (("peer memory (partials pushed over NVLink, summed in the consumer kernel)"
+                                        if args.tp_exchange == "peer" else "NCCL all-reduce") if world > 1 else None),
                        "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB streamed per token)"},
             "gpu_launches": kernels * args.steps,
             "kernels_per_step": kernels,

@@ -188,9 +188,22 @@ typedef struct {
     const void* nccl_id;    /* ncclUniqueId bytes when tp_world > 1             */
     int use_graph;          /* capture the decode step in a CUDA graph          */
     int use_pdl;            /* programmatic dependent launch between kernels    */
+    int tp_exchange;        /* VRT_TP_PEER (default) or VRT_TP_NCCL             */
+    uint32_t tp_wait_ms;    /* bound of one wait on a peer; 0 = 10000 ms        */
 } vrt_model_options;
 
-/* Defaults: max_positions 0, single GPU, use_graph = 1, use_pdl = 1. */
+/* How the partial sums of the row-parallel projections (attention output,
+ * FFN down) and the per-rank argmax keys are combined under tensor
+ * parallelism.  VRT_TP_PEER: the consuming kernel pushes its rank's partials
+ * into the peers' memory (CUDA IPC over NVLink) and sums all ranks' partials
+ * in rank order inside its prologue -- no separate collective kernel.
+ * VRT_TP_NCCL: an NCCL all-reduce after each row-parallel projection (the
+ * plain form, kept for comparison).  Both give the same sums up to fp32
+ * addition order. */
+enum { VRT_TP_PEER = 0, VRT_TP_NCCL = 1 };
+
+/* Defaults: max_positions 0, single GPU, use_graph = 1, use_pdl = 1,
+ * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0. */
 VRT_API void vrt_model_options_default(vrt_model_options* o);
 
 /* Load a Gemma 3 Q8_0 GGUF: weights repacked into the device arena, norms,

@@ -1,6 +1,9 @@
 """Tensor parallelism on 2+ B200s: TP=N against TP=1 on the same seeded
 model (hidden states within atol/rtol 1e-3, greedy ids equal unless the TP=1
-top-2 margin is below 1e-3).  Skipped on a single-GPU box."""
+top-2 margin is below 1e-3), for the peer-memory exchange (whose ranks must
+also agree bit for bit) and the NCCL one; and the peer exchange's bounded
+wait ending in VRT_E_TIMEOUT when a rank sits out a step.  Skipped on a
+single-GPU box."""
 
 import os
 import subprocess
@@ -20,13 +23,28 @@ def gpus() -> int:
         return 0
 
 
-@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("shape", ["tiny-gqa", "27b-slice"])
-def test_tp2_matches_single_gpu(shape):
+def run_worker(shape: str, mode: str, world: int = 2) -> None:
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29531",
-           os.path.join(HERE, "tp_worker.py"), shape, "77", "12"]
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", "29531",
+           os.path.join(HERE, "tp_worker.py"), shape, "77", "12", mode]
     p = subprocess.run(cmd, capture_output=True, text=True, env=env)
     print(p.stdout[-3000:], p.stderr[-3000:])
     assert p.returncode == 0
+
+
+@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("shape,mode", [("tiny-gqa", "peer"), ("27b-slice", "peer"), ("tiny-gqa", "nccl"),
+                                        ("27b-slice", "nccl")])
+def test_tp2_matches_single_gpu(shape, mode):
+    run_worker(shape, mode)
+
+
+@pytest.mark.skipif(gpus() < 4, reason="needs 4 GPUs")
+def test_tp4_peer_matches_single_gpu():
+    run_worker("27b-slice", "peer", 4)
+
+
+@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
+def test_tp2_peer_wait_times_out():
+    run_worker("tiny-gqa", "peer-timeout")

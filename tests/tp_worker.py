@@ -1,8 +1,19 @@
 """Worker for the tensor-parallel tests, one process per rank (launched by
-torchrun from tests/test_gpu_tp.py).  Rank 0 also runs the same model on a
-single GPU-worth of shards (TP=1) and compares hidden states and greedy ids.
+torchrun from tests/test_gpu_tp.py).
 
-Usage: torchrun --nproc-per-node N tests/tp_worker.py <shape> <seed> <steps>
+Modes:
+  peer, nccl   -- the TP=N model (peer-memory or NCCL exchange) decodes a
+                  prompt and a greedy continuation; rank 0 also runs the same
+                  seeded model unsharded (TP=1) and compares hidden states and
+                  greedy ids.  With the peer exchange every rank must also
+                  hold bit-identical hidden states (ranks sum in one order).
+  peer-timeout -- failure detection without a GPU fault: after two joint
+                  steps rank 1 sits out one step (between steps, nothing in
+                  flight); rank 0's exchange waits run out after 1 s and its
+                  decode call must fail with VRT_E_TIMEOUT, after which its
+                  context must still run a single-GPU model.
+
+Usage: torchrun --nproc-per-node N tests/tp_worker.py <shape> <seed> <steps> [mode]
 """
 
 import datetime
@@ -19,9 +30,34 @@ sys.path[:0] = [os.path.join(ROOT, "vortex-rt_b200"), os.path.join(ROOT, "oracle
 import synth_gguf as sg  # noqa: E402
 import vrt  # noqa: E402
 
+VRT_E_TIMEOUT = -7
+
+
+def compare_with_single_gpu(ctx, cfg, seed, toks, steps, hs, gen, world):
+    ref = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64)
+    hr = [ref.decode(t, p, 1)[0] for p, t in enumerate(toks)]
+    err = max(float(np.max(np.abs(a.astype(np.float64) - b) / (1e-3 + 1e-3 * np.abs(b)))) for a, b in zip(hs, hr))
+    gr = ref.generate(toks, steps)
+    same = gen == gr
+    print(f"TP{world} vs TP1: worst err/bound {err:.3g}; greedy ids equal: {same}", flush=True)
+    ok = err <= 1.0
+    if not same:
+        # allowed only where the TP1 top-2 margin is tiny: report the first divergence
+        i = next(i for i, (a, b) in enumerate(zip(gen, gr)) if a != b)
+        ref.reset()
+        for p, t in enumerate(toks + gr[:i]):
+            ref.decode(t, p, 1)
+        lg = ref.logits()
+        top2 = np.sort(lg)[-2:]
+        print(f"first divergence at {i}, TP1 margin {top2[1] - top2[0]:.3g}", flush=True)
+        ok = ok and (top2[1] - top2[0] < 1e-3)
+    ref.close()
+    return ok
+
 
 def main():
     shape_name, seed, steps = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
+    mode = sys.argv[4] if len(sys.argv) > 4 else "peer"
     shape = sg.SHAPES["27b"].with_(block_count=6, vocab_size=16384) if shape_name == "27b-slice" else sg.SHAPES[shape_name]
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -30,30 +66,43 @@ def main():
     dist.broadcast_object_list(obj, src=0)
     cfg = vrt.Gemma3Config.from_shape(shape)
     ctx = vrt.Context(local)
-    m = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64, tp_rank=rank, tp_world=world, nccl_id=obj[0])
+    exchange = "nccl" if mode == "nccl" else "peer"
+    m = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64, tp_rank=rank, tp_world=world,
+                  nccl_id=obj[0], tp_exchange=exchange, tp_wait_ms=1000 if mode == "peer-timeout" else 0)
     toks = [2] + np.random.default_rng(seed).integers(3, shape.vocab_size, 7).tolist()
-    hs = [m.decode(t, p, 1)[0] for p, t in enumerate(toks)]
-    gen = m.generate(toks, steps)
     ok = True
-    if rank == 0:
-        ref = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64)
-        hr = [ref.decode(t, p, 1)[0] for p, t in enumerate(toks)]
-        err = max(float(np.max(np.abs(a.astype(np.float64) - b) / (1e-3 + 1e-3 * np.abs(b)))) for a, b in zip(hs, hr))
-        gr = ref.generate(toks, steps)
-        same = gen == gr
-        print(f"TP{world} vs TP1: worst err/bound {err:.3g}; greedy ids equal: {same}", flush=True)
-        ok = err <= 1.0
-        if not same:
-            # allowed only where the TP1 top-2 margin is tiny: report the first divergence
-            i = next(i for i, (a, b) in enumerate(zip(gen, gr)) if a != b)
-            ref.reset()
-            for p, t in enumerate(toks + gr[:i]):
-                ref.decode(t, p, 1)
-            lg = ref.logits()
-            top2 = np.sort(lg)[-2:]
-            print(f"first divergence at {i}, TP1 margin {top2[1] - top2[0]:.3g}", flush=True)
-            ok = ok and (top2[1] - top2[0] < 1e-3)
-        ref.close()
+    if mode == "peer-timeout":
+        for p, t in enumerate(toks[:2]):
+            m.decode(t, p, 1)
+        dist.barrier()
+        if rank == 0:
+            try:
+                m.decode(toks[2], 2, 1)
+                print("rank 0: step without its peer did not fail", flush=True)
+                ok = False
+            except vrt.VrtError as e:
+                print(f"rank 0: {e}", flush=True)
+                ok = e.code == VRT_E_TIMEOUT
+            # the context is still usable: a single-GPU model decodes on it
+            ref = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64)
+            h, ids, _ = ref.decode(toks[0], 0, 1)
+            ok = ok and bool(np.all(np.isfinite(h))) and 0 <= ids[0] < shape.vocab_size
+            ref.close()
+        dist.barrier()
+    else:
+        hs = [m.decode(t, p, 1)[0] for p, t in enumerate(toks)]
+        gen = m.generate(toks, steps)
+        if mode == "peer":
+            # every rank holds the same residual stream bit for bit
+            mine = torch.tensor(np.stack(hs), device="cuda")
+            every = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(every, mine)
+            same = all(torch.equal(every[0], x) for x in every[1:])
+            if rank == 0:
+                print(f"hidden states identical on all ranks: {same}", flush=True)
+            ok = same
+        if rank == 0:
+            ok = compare_with_single_gpu(ctx, cfg, seed, toks, steps, hs, gen, world) and ok
     m.close()
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)

@@ -19,6 +19,7 @@
 //              index, NaN skipped), the fused tied LM head + argmax.
 #pragma once
 
+#include "tp_exchange.cuh"
 #include "vrt_device.cuh"
 
 namespace vrt {
@@ -55,6 +56,9 @@ struct GemvParams {
     // next kernel (same partition rule, next_group: group-granular spans).
     const uint8_t* next_w;
     uint32_t next_rows, next_cols, next_grid, next_group, pf_bytes;
+    // Resid*: tensor-parallel exchange of the block output (tp.world > 1);
+    // x then points at tp.sum, which this launch fills before its prologue.
+    TpParams tp;
 };
 
 // First tile of CTA b's span under the partition rule of the kernel below.
@@ -174,11 +178,12 @@ __device__ __forceinline__ void norm_prologue(const GemvParams& p, float* xs, do
     const float4* wq4 = reinterpret_cast<const float4*>(p.w_pre);
     float4 a[kPrologueVec], b[kPrologueVec], c[kPrologueVec], w[kPrologueVec];
     const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool l2_only = p.tp.world > 1;  // x written by other CTAs of this grid
 #pragma unroll
     for (int u = 0; u < kPrologueVec; ++u) {
         const uint32_t i = ctid + u * NC;
         const bool ok = i < n4;
-        a[u] = ok ? x4[i] : z;
+        a[u] = ok ? (l2_only ? __ldcg(x4 + i) : x4[i]) : z;
         w[u] = ok ? wq4[i] : z;
         if (PRO != kProRmsInto) {
             b[u] = ok ? h4[i] : z;
@@ -320,6 +325,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
     }
     for (int i = ctid; i < 2 * kConsumerWarps * kChunkGroups * 16; i += NC) partial[i] = 0.0f;
 
+    if (PRO == kProResid || PRO == kProResidFinal) {
+        if (p.tp.world > 1) {
+            // sum the ranks' partials of the block output: this CTA's slice,
+            // then a grid barrier so every CTA can read the whole vector
+            const uint32_t seq = tp_seq(p.tp);
+            const uint32_t a = static_cast<uint64_t>(p.tp.n) * blockIdx.x / gridDim.x;
+            const uint32_t e = static_cast<uint64_t>(p.tp.n) * (blockIdx.x + 1) / gridDim.x;
+            tp_slice_reduce(p.tp, seq, a, e, ctid, NC, p.status);
+            named_bar_sync(1, NC);
+            if (ctid == 0) tp_grid_barrier(p.tp, seq, p.status);
+            named_bar_sync(1, NC);
+        }
+    }
+
     const uint32_t K = p.cols, nblk = K / 32;
     if (PRO == kProPlain) {
         // blocks of 32 activations: all loads of a thread issued before use
@@ -367,14 +386,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
             double so = 0.0;
             float ps = 1.0f;
             if (PRO != kProRmsInto) {
-                for (uint32_t k = ctid; k < K; k += NC) so += static_cast<double>(p.x[k]) * p.x[k];
+                for (uint32_t k = ctid; k < K; k += NC) so += static_cast<double>(__ldcg(p.x + k)) * __ldcg(p.x + k);
                 so = consumer_sum(so, red);
                 ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(K)) + p.eps);
             }
             double ss = 0.0;
             for (uint32_t k = ctid; k < K; k += NC) {
-                const float h = PRO == kProRmsInto ? p.x[k]
-                                                   : __fadd_rn(__fmul_rn(p.x[k], __fmul_rn(ps, p.w_post[k])), p.h_prev[k]);
+                const float xk = __ldcg(p.x + k);
+                const float h = PRO == kProRmsInto ? xk : __fadd_rn(__fmul_rn(xk, __fmul_rn(ps, p.w_post[k])), p.h_prev[k]);
                 xs[k] = h;
                 ss += static_cast<double>(h) * h;
                 if (PRO != kProRmsInto && blockIdx.x == 0) {

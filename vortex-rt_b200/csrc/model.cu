@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -154,13 +155,19 @@ struct StepState {
     float result_value;
     uint32_t pad;
     unsigned long long key;
+    uint32_t epoch;  // steps run since creation; never reset (tensor-parallel exchange sequence numbers)
+    uint32_t pad2;
 };
+// Host writes (reset, prefill start) cover the fields before `epoch`.
+constexpr size_t kStepStateHostBytes = offsetof(StepState, epoch);
 
-__global__ void finalize_decode_kernel(StepState* st, uint32_t vocab, uint32_t* out_ids, uint32_t out_cap) {
+__global__ void finalize_decode_kernel(StepState* st, uint32_t vocab, uint32_t* out_ids, uint32_t out_cap,
+                                       const TpParams tp) {
     pdl_wait();
     uint32_t idx;
     float val;
-    argmax_unkey(st->key, &idx, &val);
+    const unsigned long long key = tp.world > 1 ? tp_key_max(tp, st->key, &st->status) : st->key;
+    argmax_unkey(key, &idx, &val);
     st->result_index = idx;
     st->result_value = val;
     if (idx >= vocab || !isfinite(val)) st->status |= kStatusNonFinite;
@@ -170,6 +177,7 @@ __global__ void finalize_decode_kernel(StepState* st, uint32_t vocab, uint32_t* 
     st->token = idx < vocab ? idx : 0u;
     st->pos += 1;
     st->key = 0ull;
+    st->epoch += 1;
 }
 
 __global__ void finalize_prefill_kernel(StepState* st, const uint32_t* prompt) {
@@ -177,18 +185,28 @@ __global__ void finalize_prefill_kernel(StepState* st, const uint32_t* prompt) {
     const uint32_t p = st->pos + 1;
     st->pos = p;
     if (p < st->prompt_count) st->token = prompt[p];
+    st->epoch += 1;
 }
 
 // Final residual + output norm without the LM head (top_k == 0 steps).
 __global__ void final_hidden_kernel(const float* dn, const float* h_prev, const float* w_post, const float* w_out,
-                                    float* hidden, float* trace, uint32_t d, float eps, uint32_t* status) {
+                                    float* hidden, float* trace, uint32_t d, float eps, uint32_t* status,
+                                    const TpParams tp) {
     pdl_wait();
+    if (tp.world > 1) {  // tensor parallel: sum the ranks' partials of the last FFN output first
+        tp_slice_reduce(tp, tp_seq(tp), 0, d, threadIdx.x, blockDim.x, status);
+        __syncthreads();
+        dn = tp.sum;
+    }
     __shared__ double red[32];
     __shared__ float scale_s;
     extern __shared__ float hs[];
     const int tid = threadIdx.x;
     double so = 0.0;
-    for (uint32_t k = tid; k < d; k += blockDim.x) so += static_cast<double>(dn[k]) * static_cast<double>(dn[k]);
+    for (uint32_t k = tid; k < d; k += blockDim.x) {
+        const double v = __ldcg(dn + k);
+        so += v * v;
+    }
     so = warp_sum(so);
     if ((tid & 31) == 0) red[tid / 32] = so;
     __syncthreads();
@@ -202,7 +220,7 @@ __global__ void final_hidden_kernel(const float* dn, const float* h_prev, const 
     double ss = 0.0;
     bool bad = false;
     for (uint32_t k = tid; k < d; k += blockDim.x) {
-        const float h = __fadd_rn(__fmul_rn(dn[k], __fmul_rn(ps, w_post[k])), h_prev[k]);
+        const float h = __fadd_rn(__fmul_rn(__ldcg(dn + k), __fmul_rn(ps, w_post[k])), h_prev[k]);
         hs[k] = h;
         bad |= !isfinite(h);
         if (trace) trace[k] = h;
@@ -245,6 +263,7 @@ struct Nccl {
     int (*CommDestroy)(void*) = nullptr;
     int (*GetUniqueId)(void*) = nullptr;
     const char* (*GetErrorString)(int) = nullptr;
+    int (*AllGather)(const void*, void*, size_t, int, void*, cudaStream_t) = nullptr;
 };
 
 }  // namespace vrt
@@ -279,6 +298,13 @@ struct vrt_model {
     void* comm = nullptr;
     unsigned long long* key_tmp = nullptr;
     vrt::Nccl nccl;
+    // peer-memory exchange (tp_exchange == VRT_TP_PEER, world > 1)
+    bool tp_peer = false;
+    unsigned long long* tp_slots = nullptr;             // own receive slots (exported by CUDA IPC)
+    std::vector<unsigned long long*> tp_peer_slots;     // every rank's slots, mapped here (own included)
+    unsigned long long** tp_peers_dev = nullptr;        // the same table on the device
+    float* tp_sum = nullptr;                            // reduced vectors, [2][d]
+    uint32_t* tp_bar = nullptr;                         // grid barrier counter, generation
 };
 
 namespace vrt {
@@ -295,7 +321,8 @@ static int nccl_load(Nccl& n) {
     n.CommDestroy = reinterpret_cast<decltype(n.CommDestroy)>(dlsym(n.lib, "ncclCommDestroy"));
     n.GetUniqueId = reinterpret_cast<decltype(n.GetUniqueId)>(dlsym(n.lib, "ncclGetUniqueId"));
     n.GetErrorString = reinterpret_cast<decltype(n.GetErrorString)>(dlsym(n.lib, "ncclGetErrorString"));
-    if (!n.AllReduce || !n.CommDestroy || !n.GetUniqueId || !n.GetErrorString) {
+    n.AllGather = reinterpret_cast<decltype(n.AllGather)>(dlsym(n.lib, "ncclAllGather"));
+    if (!n.AllReduce || !n.CommDestroy || !n.GetUniqueId || !n.GetErrorString || !n.AllGather) {
         return fail(VRT_E_UNSUPPORTED, "libnccl.so.2 lacks the expected symbols");
     }
     return VRT_OK;
@@ -706,6 +733,30 @@ static int nccl_sum(vrt_model* m, float* buf, size_t n, cudaStream_t s) {
     return VRT_OK;
 }
 
+// Exchange parameters of one consumer of row-parallel partial sums.  Ops are
+// numbered per step: 2l = attention output of layer l (slot set 0), 2l+1 =
+// FFN down of layer l (set 1), 2L = the argmax key.
+static TpParams tp_params(vrt_model* m, uint32_t set, uint32_t op, const float* local) {
+    TpParams t{};
+    if (!m->tp_peer) return t;
+    const uint32_t d = m->cfg.embedding_length;
+    t.peers = m->tp_peers_dev;
+    t.slots = m->tp_slots;
+    t.local = local;
+    t.sum = m->tp_sum + static_cast<uint64_t>(set) * d;
+    t.bar_count = m->tp_bar;
+    t.bar_gen = m->tp_bar + 1;
+    t.epoch = &m->st->epoch;
+    t.wait_ns = static_cast<uint64_t>(m->opt.tp_wait_ms ? m->opt.tp_wait_ms : 10000u) * 1000000ull;
+    t.rank = static_cast<uint32_t>(m->rank);
+    t.world = static_cast<uint32_t>(m->world);
+    t.set = set;
+    t.op = op;
+    t.ops_per_step = 2 * m->cfg.block_count + 1;
+    t.n = d;
+    return t;
+}
+
 // The mat-vecs of one decode step, in launch order: weight base, rows, cols,
 // and whether the epilogue partitions by whole row groups.
 struct StepGemv {
@@ -779,7 +830,8 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
                 p.emb_scale = std::sqrt(static_cast<float>(d));
                 VRT_TRY(gemv(kProEmbed, kEpiAtomic, p));
             } else {
-                p.x = m->dn;
+                p.x = m->tp_peer ? m->tp_sum + d : m->dn;
+                p.tp = tp_params(m, 1, 2 * (l - 1) + 1, m->dn);
                 p.h_prev = m->h1;
                 p.w_post = F(m->layers[l - 1].n_post_ffw);
                 p.trace = trace ? trace + static_cast<uint64_t>(l - 1) * d : nullptr;
@@ -825,7 +877,7 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
             p.zero0 = m->qkv;
             p.zero0_count = m->qwl + 2 * m->kwl;
             VRT_TRY(gemv(kProPlain, kEpiAtomic, p));
-            VRT_TRY(nccl_sum(m, m->o, d, s));
+            if (!m->tp_peer) VRT_TRY(nccl_sum(m, m->o, d, s));
         }
         // gate/up with residual + post-attention norm + ffn norm
         {
@@ -833,7 +885,8 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
             p.w = m->arena + L.gu;
             p.rows = 2 * m->ffl;
             p.cols = d;
-            p.x = m->o;
+            p.x = m->tp_peer ? m->tp_sum : m->o;
+            p.tp = tp_params(m, 0, 2 * l, m->o);
             p.h_prev = m->h0;
             p.w_post = F(L.n_post_attn);
             p.w_pre = F(L.n_ffn);
@@ -852,7 +905,7 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
             p.zero0 = m->o;
             p.zero0_count = d;
             VRT_TRY(gemv(kProPlain, kEpiAtomic, p));
-            VRT_TRY(nccl_sum(m, m->dn, d, s));
+            if (!m->tp_peer) VRT_TRY(nccl_sum(m, m->dn, d, s));
         }
     }
     const auto& last = m->layers[c.block_count - 1];
@@ -863,7 +916,8 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
         p.w = m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes;
         p.rows = m->vocab_hi - m->vocab_lo;
         p.cols = d;
-        p.x = m->dn;
+        p.x = m->tp_peer ? m->tp_sum + d : m->dn;
+        p.tp = tp_params(m, 1, 2 * c.block_count - 1, m->dn);
         p.h_prev = m->h1;
         p.w_post = F(last.n_post_ffw);
         p.w_pre = F(m->out_norm);
@@ -873,17 +927,17 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
         p.amax = &m->st->key;
         p.row_base = m->vocab_lo;
         VRT_TRY(gemv(kProResidFinal, kEpiArgmax, p));
-        if (m->world > 1) {
+        if (m->world > 1 && !m->tp_peer) {
             const int r = m->nccl.AllReduce(&m->st->key, &m->st->key, 1, /*ncclUint64*/ 5, /*ncclMax*/ 2, m->comm, s);
             if (r) return fail(VRT_E_CUDA, "ncclAllReduce(max) failed: %s", m->nccl.GetErrorString(r));
         }
-        VRT_CUDA(launch(finalize_decode_kernel, dim3(1), dim3(1), 0, s, pdl && m->world <= 1, m->st,
-                        c.vocab_size, m->out_ids, kMaxSteps));
+        VRT_CUDA(launch(finalize_decode_kernel, dim3(1), dim3(1), 0, s, pdl && (m->world <= 1 || m->tp_peer), m->st,
+                        c.vocab_size, m->out_ids, kMaxSteps, tp_params(m, 0, 2 * c.block_count, nullptr)));
         nk += 1;
     } else {
         VRT_CUDA(launch(final_hidden_kernel, dim3(1), dim3(1024), d * 4, s, pdl, (const float*)m->dn,
                         (const float*)m->h1, F(last.n_post_ffw), F(m->out_norm), m->hidden, tlast, d, c.rms_epsilon,
-                        status));
+                        status, tp_params(m, 1, 2 * c.block_count - 1, m->dn)));
         VRT_CUDA(launch(finalize_prefill_kernel, dim3(1), dim3(1), 0, s, pdl, m->st, (const uint32_t*)m->prompt));
         nk += 2;
     }
@@ -925,6 +979,73 @@ static int run_step(vrt_model* m, bool head) {
     return record_step(m, s, head, nullptr);
 }
 
+// Peer-memory exchange set-up: allocate and export this rank's receive
+// slots, gather every rank's CUDA IPC handle with one NCCL all-gather, map
+// the peers' slots (NVLink peer access).
+static int tp_peer_setup(vrt_model* m) {
+    const uint32_t d = m->cfg.embedding_length, W = static_cast<uint32_t>(m->world);
+    cudaStream_t s = m->ctx->stream;
+    const uint64_t bytes = tp_slot_words(W, d) * 8;
+    VRT_CUDA(cudaMalloc(&m->tp_slots, bytes));
+    VRT_CUDA(cudaMemsetAsync(m->tp_slots, 0, bytes, s));
+    VRT_CUDA(cudaMalloc(&m->tp_sum, 2ull * d * 4 + 256));
+    VRT_CUDA(cudaMemsetAsync(m->tp_sum, 0, 2ull * d * 4 + 256, s));
+    m->tp_bar = reinterpret_cast<uint32_t*>(m->tp_sum + 2ull * d);
+    cudaIpcMemHandle_t h;
+    VRT_CUDA(cudaIpcGetMemHandle(&h, m->tp_slots));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t* dh = nullptr;
+    VRT_CUDA(cudaMalloc(&dh, 64ull * W));
+    std::vector<cudaIpcMemHandle_t> hs(W);
+    cudaError_t e = cudaMemcpyAsync(dh + 64ull * m->rank, &h, 64, cudaMemcpyHostToDevice, s);
+    const int r = e == cudaSuccess ? m->nccl.AllGather(dh + 64ull * m->rank, dh, 64, /*ncclUint8*/ 1, m->comm, s) : 0;
+    if (e == cudaSuccess && !r) e = cudaMemcpyAsync(hs.data(), dh, 64ull * W, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && !r) e = cudaStreamSynchronize(s);
+    cudaFree(dh);
+    if (r) return fail(VRT_E_CUDA, "ncclAllGather failed: %s", m->nccl.GetErrorString(r));
+    if (e != cudaSuccess) return cuda_fail(e, "IPC handle exchange", __FILE__, __LINE__);
+    m->tp_peer_slots.assign(W, nullptr);
+    for (uint32_t q = 0; q < W; ++q) {
+        if (q == static_cast<uint32_t>(m->rank)) {
+            m->tp_peer_slots[q] = m->tp_slots;
+            continue;
+        }
+        void* ptr = nullptr;
+        e = cudaIpcOpenMemHandle(&ptr, hs[q], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            return fail(VRT_E_UNSUPPORTED, "tensor parallelism: cannot map rank %u's memory (%s); tp_exchange = VRT_TP_NCCL "
+                        "works without peer access", q, cudaGetErrorString(e));
+        }
+        m->tp_peer_slots[q] = static_cast<unsigned long long*>(ptr);
+    }
+    VRT_CUDA(cudaMalloc(&m->tp_peers_dev, 8ull * W));
+    VRT_CUDA(cudaMemcpy(m->tp_peers_dev, m->tp_peer_slots.data(), 8ull * W, cudaMemcpyHostToDevice));
+    m->tp_peer = true;
+    return VRT_OK;
+}
+
+// All ranks stop touching each other's slots before any rank unmaps or
+// frees them (an NCCL all-reduce of one float on each side).
+static void tp_peer_teardown(vrt_model* m) {
+    cudaStream_t s = m->ctx->stream;
+    auto barrier = [&] {
+        if (m->tp_peer && m->comm && m->tp_sum) {
+            m->nccl.AllReduce(m->tp_sum, m->tp_sum, 1, /*ncclFloat32*/ 7, /*ncclSum*/ 0, m->comm, s);
+            cudaStreamSynchronize(s);
+        }
+    };
+    barrier();
+    for (size_t q = 0; q < m->tp_peer_slots.size(); ++q) {
+        if (m->tp_peer_slots[q] && m->tp_peer_slots[q] != m->tp_slots) cudaIpcCloseMemHandle(m->tp_peer_slots[q]);
+    }
+    barrier();
+    m->tp_peer_slots.clear();
+    m->tp_peer = false;
+    cudaFree(m->tp_peers_dev);
+    cudaFree(m->tp_sum);
+    cudaFree(m->tp_slots);
+}
+
 static int finish_create(vrt_model* m) {
     if (m->world > 1) {
         VRT_TRY(nccl_load(m->nccl));
@@ -934,6 +1055,7 @@ static int finish_create(vrt_model* m) {
         memcpy(id.b, m->opt.nccl_id, 128);
         const int r = init(&m->comm, m->world, id, m->rank);
         if (r) return fail(VRT_E_CUDA, "ncclCommInitRank failed: %s", m->nccl.GetErrorString(r));
+        if (m->opt.tp_exchange == VRT_TP_PEER) VRT_TRY(tp_peer_setup(m));
     }
     VRT_TRY(build_graphs(m));
     return VRT_OK;
@@ -945,6 +1067,7 @@ static void destroy_model(vrt_model* m) {
     cudaStreamSynchronize(m->ctx->stream);
     if (m->g_head) cudaGraphExecDestroy(m->g_head);
     if (m->g_nohead) cudaGraphExecDestroy(m->g_nohead);
+    tp_peer_teardown(m);
     if (m->comm && m->nccl.CommDestroy) m->nccl.CommDestroy(m->comm);
     cudaFree(m->arena);
     cudaFree(m->kv_mem);
@@ -971,6 +1094,9 @@ static int begin_model(vrt_ctx* ctx, const vrt_model_options* opts, vrt_model** 
     if (m->world > 1 && (m->rank < 0 || m->rank >= m->world || !m->opt.nccl_id)) {
         return fail(VRT_E_INVALID, "tensor-parallel rank/world/nccl_id invalid");
     }
+    if (m->opt.tp_exchange != VRT_TP_PEER && m->opt.tp_exchange != VRT_TP_NCCL) {
+        return fail(VRT_E_INVALID, "tp_exchange must be VRT_TP_PEER or VRT_TP_NCCL");
+    }
     VRT_CUDA(cudaSetDevice(ctx->device));
     VRT_CUDA(gemv_init_attributes());
     return VRT_OK;
@@ -979,10 +1105,12 @@ static int begin_model(vrt_ctx* ctx, const vrt_model_options* opts, vrt_model** 
 static int device_status(vrt_model* m, uint32_t& status) {
     status = m->st_host->status;
     if (!status) return VRT_OK;
-    const char* what = (status & kStatusWaitTimeout) ? "a bounded device wait timed out"
-                       : (status & kStatusBadToken)  ? "Token id is outside Gemma 3 vocabulary"
-                                                     : "Non-finite value in the Gemma 3 hidden state or logits";
-    return fail((status & kStatusWaitTimeout) ? VRT_E_TIMEOUT : VRT_E_NUMERIC, "%s (device status 0x%x)", what, status);
+    const bool timeout = (status & (kStatusWaitTimeout | kStatusPeerTimeout)) != 0u;
+    const char* what = (status & kStatusPeerTimeout)   ? "a tensor-parallel peer did not answer in time"
+                       : (status & kStatusWaitTimeout) ? "a bounded device wait timed out"
+                       : (status & kStatusBadToken)    ? "Token id is outside Gemma 3 vocabulary"
+                                                       : "Non-finite value in the Gemma 3 hidden state or logits";
+    return fail(timeout ? VRT_E_TIMEOUT : VRT_E_NUMERIC, "%s (device status 0x%x)", what, status);
 }
 
 }  // namespace vrt
@@ -1066,8 +1194,9 @@ int vrt_model_reset(vrt_model* m) {
     if (!m) return fail(VRT_E_INVALID, "null model");
     VRT_CUDA(cudaSetDevice(m->ctx->device));
     VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
-    memset(m->st_host, 0, sizeof(StepState));
-    VRT_CUDA(cudaMemcpyAsync(m->st, m->st_host, sizeof(StepState), cudaMemcpyHostToDevice, m->ctx->stream));
+    memset(m->st_host, 0, kStepStateHostBytes);
+    VRT_CUDA(cudaMemcpyAsync(m->st, m->st_host, kStepStateHostBytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    if (m->tp_bar) VRT_CUDA(cudaMemsetAsync(m->tp_bar, 0, 8, m->ctx->stream));
     VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
     m->next_pos = 0;
     m->generated = 0;
@@ -1096,7 +1225,7 @@ int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t to
     sh->prompt_count = 0;
     VRT_CUDA(cudaMemcpyAsync(m->st, sh, 20, cudaMemcpyHostToDevice, s));
     VRT_TRY(run_step(m, top_k > 0));
-    VRT_CUDA(cudaMemcpyAsync(sh, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaMemcpyAsync(sh, m->st, kStepStateHostBytes, cudaMemcpyDeviceToHost, s));
     if (h_hidden) VRT_CUDA(cudaMemcpyAsync(m->hidden_host, m->hidden, 4ull * c.embedding_length, cudaMemcpyDeviceToHost, s));
     std::vector<float> logits;
     if (top_k > 1) {
@@ -1158,10 +1287,10 @@ int vrt_prefill(vrt_model* m, const uint32_t* h_prompt, uint32_t n) {
     VRT_CUDA(cudaStreamSynchronize(s));
     VRT_CUDA(cudaMemcpyAsync(m->prompt, h_prompt, 4ull * n, cudaMemcpyHostToDevice, s));
     StepState* sh = m->st_host;
-    memset(sh, 0, sizeof(StepState));
+    memset(sh, 0, kStepStateHostBytes);
     sh->token = h_prompt[0];
     sh->prompt_count = n;
-    VRT_CUDA(cudaMemcpyAsync(m->st, sh, sizeof(StepState), cudaMemcpyHostToDevice, s));
+    VRT_CUDA(cudaMemcpyAsync(m->st, sh, kStepStateHostBytes, cudaMemcpyHostToDevice, s));
     for (uint32_t i = 0; i + 1 < n; ++i) VRT_TRY(run_step(m, false));
     VRT_TRY(run_step(m, true));
     VRT_CUDA(cudaMemcpyAsync(sh, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, s));
