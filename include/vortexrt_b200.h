@@ -169,6 +169,19 @@ VRT_API int vrt_q8t_gate_up(vrt_ctx* ctx, const void* d_packed_pair, uint32_t ff
 VRT_API int vrt_q8t_ffn(vrt_ctx* ctx, const void* d_gate_up, const void* d_down, uint32_t input_dim,
                         uint32_t ffn_dim, uint32_t output_dim, const float* d_x, float* d_act, float* d_y,
                         void* stream);
+/* Tensor-core (tcgen05) GEMM over a packed matrix: d_y[m][rows] = d_x[m][cols] . W^T
+ * for m activation rows (prompt tokens or batched sequences), rows % 128 == 0.
+ * Operands are split into fp16 hi + lo terms (three MMAs, fp32 accumulation:
+ * ~1e-7 relative error).  Synchronous; uses a context scratch of
+ * 4*m*cols bytes.  No reference counterpart: the reference runs every prompt
+ * token through the mat-vec path (src/gemma3.cpp:2080-2149). */
+VRT_API int vrt_q8t_gemm(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint32_t cols, const float* d_x,
+                         uint32_t m, float* d_y, void* stream);
+/* Gate/up pair form (d_packed_pair from vrt_q8t_pack_pair, ffn % 64 == 0):
+ * d_act[m][ffn] = gelu_tanh(gate) * up, the batched run_staged_ffn first half
+ * (src/q8_matvec.cpp:1360-2004 per token). */
+VRT_API int vrt_q8t_gemm_gelu(vrt_ctx* ctx, const void* d_packed_pair, uint32_t ffn, uint32_t cols,
+                              const float* d_x, uint32_t m, float* d_act, void* stream);
 /* LM head + argmax over a packed vocab matrix (logits written when d_logits != NULL). */
 VRT_API int vrt_q8t_lm_head_argmax(vrt_ctx* ctx, const void* d_packed, uint32_t vocab, uint32_t cols,
                                    const float* d_x, float* d_logits, vrt_argmax_result* d_out, void* stream);

@@ -1,0 +1,173 @@
+// Host side of the tensor-core Q8_0 GEMM (gemm_q8t.cuh): TMA tensor maps for
+// the fp16 hi/lo activation operands, the launcher used by the model's
+// batched paths, and the packed-matrix C ABI entry points.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "gemm_q8t.cuh"
+#include "vrt_internal.hpp"
+#include "vrt_kernels.hpp"
+
+namespace vrt {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    });
+    return fn;
+}
+
+// Tensor map over a row-major fp16 matrix [rows][cols] (cols % 64 == 0, base
+// 16-byte aligned), box = 64 columns x 128 rows, 128B swizzle; rows past the
+// end read as zeros.
+int make_f16_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols) {
+    static_assert(sizeof(TmaMap) == sizeof(CUtensorMap), "tensor map size");
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(VRT_E_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
+    if (cols % kGemmBK || reinterpret_cast<uintptr_t>(base) % 16) return fail(VRT_E_INVALID, "fp16 operand layout");
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), static_cast<cuuint32_t>(kGemmBM)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VRT_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return VRT_OK;
+}
+
+template <int EPI>
+static cudaError_t gemm_launch_t(const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
+    static uint64_t done = 0;  // devices whose attribute is set (bit per ordinal)
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && !(done & (1ull << dev))) {
+        e = cudaFuncSetAttribute(q8t_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes);
+        if (e != cudaSuccess) return e;
+        done |= 1ull << dev;
+    }
+    const dim3 grid(p.n / kGemmBN, (p.m + kGemmBM - 1) / kGemmBM);
+    return launch(q8t_gemm_kernel<EPI>, grid, dim3(kGemmThreads), kGemmSmemBytes, s, false, hi, lo, p);
+}
+
+cudaError_t gemm_q8t(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
+    return epi == kGemmStore ? gemm_launch_t<kGemmStore>(hi, lo, p, s) : gemm_launch_t<kGemmGeluSplit>(hi, lo, p, s);
+}
+
+// Split fp32 rows into fp16 hi/lo operands (x = hi + lo to ~2^-22 relative).
+__global__ void split_f16_kernel(const float* __restrict__ x, uint64_t n, __half* __restrict__ hi,
+                                 __half* __restrict__ lo) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        __half h, l;
+        split_f16(x[i], h, l);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+cudaError_t split_f16(const float* x, uint64_t n, __half* hi, __half* lo, cudaStream_t s) {
+    const uint64_t blocks = (n + 255) / 256;
+    split_f16_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(x, n, hi, lo);
+    return cudaGetLastError();
+}
+
+// Context scratch of at least `bytes` (grown by reallocation; not shared
+// between concurrent calls on one context).
+static int ctx_workspace(vrt_ctx* ctx, size_t bytes, void** out) {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    if (ctx->ws_bytes < bytes) {
+        if (ctx->ws) {
+            VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+            VRT_CUDA(cudaFree(ctx->ws));
+            ctx->ws = nullptr;
+            ctx->ws_bytes = 0;
+        }
+        VRT_CUDA(cudaMalloc(&ctx->ws, bytes));
+        ctx->ws_bytes = bytes;
+    }
+    *out = ctx->ws;
+    return VRT_OK;
+}
+
+static int gemm_common(vrt_ctx* ctx, int epi, const void* d_packed, uint32_t rows, uint32_t cols, const float* d_x,
+                       uint32_t m, float* d_out, void* stream) {
+    if (!ctx || !d_packed || !d_x || !d_out) return fail(VRT_E_INVALID, "null argument");
+    if (!m || !rows || rows % kGemmBN || !cols || cols % kTileCols) {
+        return fail(VRT_E_INVALID, "tensor-core GEMM needs rows %% 128 == 0, cols %% 128 == 0, m > 0");
+    }
+    if (reinterpret_cast<uintptr_t>(d_packed) % 16) return fail(VRT_E_INVALID, "packed weights must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(d_out) % 16) return fail(VRT_E_INVALID, "output must be 16-byte aligned");
+    cudaStream_t s = as_stream(ctx, stream);
+    VRT_CUDA(cudaSetDevice(ctx->device));
+    const uint64_t xn = static_cast<uint64_t>(m) * cols;
+    const uint64_t an = epi == kGemmGeluSplit ? static_cast<uint64_t>(m) * (rows / 2) : 0;
+    void* ws = nullptr;
+    VRT_TRY(ctx_workspace(ctx, (2 * xn + 2 * an) * sizeof(__half) + 256, &ws));
+    __half* xh = static_cast<__half*>(ws);
+    __half* xl = xh + xn;
+    VRT_CUDA(split_f16(d_x, xn, xh, xl, s));
+    TmaMap th, tl;
+    VRT_TRY(make_f16_tmap(&th, xh, m, cols));
+    VRT_TRY(make_f16_tmap(&tl, xl, m, cols));
+    GemmParams p{};
+    p.w = static_cast<const uint8_t*>(d_packed);
+    p.n = rows;
+    p.k = cols;
+    p.m = m;
+    uint32_t* status = reinterpret_cast<uint32_t*>(ctx->d_key + 1);  // word after the argmax key
+    p.status = status;
+    if (epi == kGemmStore) {
+        p.y = d_out;
+        p.ldy = rows;
+    } else {
+        p.act_hi = xl + xn;
+        p.act_lo = p.act_hi + an;
+        p.act_f32 = d_out;
+        p.ld_act = rows / 2;
+    }
+    VRT_CUDA(cudaMemsetAsync(status, 0, 4, s));
+    VRT_CUDA(gemm_q8t(epi, th, tl, p, s));
+    uint32_t st = 0;
+    VRT_CUDA(cudaMemcpyAsync(&st, status, 4, cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    if (st) return fail(VRT_E_TIMEOUT, "tensor-core GEMM: a bounded device wait timed out");
+    return VRT_OK;
+}
+
+}  // namespace vrt
+
+using namespace vrt;
+
+extern "C" {
+
+int vrt_q8t_gemm(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint32_t cols, const float* d_x, uint32_t m,
+                 float* d_y, void* stream) {
+    clear_error();
+    return gemm_common(ctx, kGemmStore, d_packed, rows, cols, d_x, m, d_y, stream);
+}
+
+int vrt_q8t_gemm_gelu(vrt_ctx* ctx, const void* d_packed_pair, uint32_t ffn, uint32_t cols, const float* d_x,
+                      uint32_t m, float* d_act, void* stream) {
+    clear_error();
+    if (ffn % 64) return fail(VRT_E_INVALID, "tensor-core gate/up needs ffn %% 64 == 0");
+    return gemm_common(ctx, kGemmGeluSplit, d_packed_pair, 2 * ffn, cols, d_x, m, d_act, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,375 @@
+// Q8_0 x activation GEMM on the 5th-generation tensor cores (tcgen05), sm_100a.
+//
+// Y[m][n] = sum_k X[m][k] * W[n][k] for M activation rows (prompt tokens or
+// batched sequences) against a Q8T-tiled Q8_0 matrix W [N][K].  Q8_0 carries
+// one fp16 scale per 32 weights along K for every row, which no tensor-core
+// format can apply inside the accumulation, so the weights are dequantised
+// on chip: w = scale * q is exact in fp32 (11 + 7 significant bits) and is
+// split into two fp16 terms, w = w_hi + w_lo; the activations are split the
+// same way.  Three MMAs per K step (x_hi.w_hi + x_lo.w_hi + x_hi.w_lo) into
+// one fp32 TMEM accumulator leave a relative error near 1e-7, far inside the
+// 1e-3 tolerance the fp32 reference path is held to (a single fp16 product
+// would sit near 3e-4).
+//
+// The tensor core's fp32 accumulation truncates at every MMA, a bias that
+// grows linearly with the number of MMAs into one accumulator (4e-4 relative
+// at K = 21504 measured on B200).  So the K loop is cut into chunks of 256
+// columns: each chunk accumulates into one of two TMEM accumulators (ping-
+// pong), and a dedicated epilogue warpgroup drains every finished chunk into
+// fp32 registers with round-to-nearest adds while the MMAs fill the other.
+//
+// One CTA computes a 128 (M) x 128 (N) tile.  Warp roles:
+//   warp 0    producer: 2-D TMA loads (128B swizzle) of the x_hi / x_lo tiles
+//             (64 K columns x 128 rows each) into the operand ring, and 1-D
+//             bulk copies of the Q8T weight tiles (8 row groups x 128 K
+//             columns, 17,408 bytes) into the raw ring;
+//   warp 1    TMEM allocation; lane 0 issues tcgen05.mma (kind::f16, fp32
+//             accumulate, both operands K-major) and tcgen05.commit;
+//   warps 2-5 dequantise each raw stage into the w_hi / w_lo operand tiles in
+//             the canonical K-major 128B-swizzled layout;
+//   warps 6-13 epilogue: tcgen05.ld of each finished chunk accumulator (warp
+//             w owns the 32 TMEM lanes = output rows of quarter w % 4 and 64
+//             of the 128 columns), running fp32 sums in registers, then the
+//             fused output stage.
+// Every mbarrier wait is bounded; TMEM is always freed before exit.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "vrt_device.cuh"
+
+namespace vrt {
+
+enum GemmEpi : int {
+    kGemmStore = 0,      // y[m][n] fp32
+    kGemmGeluSplit = 1,  // W rows are 8 gate + 8 up per group: act = gelu(gate) * up -> fp16 hi/lo (+ optional fp32)
+};
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBN = 128;
+constexpr int kGemmBK = 64;                                   // fp16 columns per operand stage (one 128-byte row)
+constexpr int kGemmStages = 2;                                // operand ring
+constexpr int kGemmRawStages = 2;                             // Q8T weight ring
+constexpr int kGemmOpTile = kGemmBM * kGemmBK * 2;            // 16 KB: one 128 x 64 fp16 operand
+constexpr int kGemmStageBytes = 4 * kGemmOpTile;              // x_hi, x_lo, w_hi, w_lo
+constexpr int kGemmRawBytes = (kGemmBN / kTileRows) * kTileBytes;  // 17,408
+constexpr int kGemmThreads = 448;
+constexpr int kGemmEpiCols = 64;                              // accumulator columns per epilogue warp
+constexpr int kGemmChunkStages = 4;                           // operand stages (256 K columns) per accumulator chunk
+constexpr uint32_t kGemmSmemBytes =
+    1024 + kGemmStages * kGemmStageBytes + kGemmRawStages * kGemmRawBytes + 8 * (2 * kGemmStages + 2 * kGemmRawStages + 4) + 16;
+
+// CUtensorMap storage (the driver's opaque 128-byte tensor map).
+struct alignas(64) TmaMap {
+    unsigned long long raw[16];
+};
+
+struct GemmParams {
+    const uint8_t* w;     // Q8T matrix, N rows x K columns
+    uint32_t n, k, m;     // N % 128 == 0, K % 128 == 0, M >= 1
+    float* y;             // Store: y[m * ldy + n]
+    uint32_t ldy;
+    __half* act_hi;       // GeluSplit: act_*[m * ld_act + n / 2]
+    __half* act_lo;
+    float* act_f32;       // GeluSplit: optional fp32 copy
+    uint32_t ld_act;
+    uint32_t* status;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const TmaMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, M = 128, N = 128, K = 16, fp16 inputs, fp32 accumulate.
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on `bar` when all tcgen05.mma issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand of 128-byte rows, 8-row
+// swizzle atoms of 1024 bytes stacked contiguously, 128B swizzle (layout 2),
+// descriptor version 1, leading-byte offset 1 (unused for swizzled K-major).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, N = 128, M = 128.
+constexpr uint32_t kGemmIdesc = (1u << 4) | (static_cast<uint32_t>(kGemmBN >> 3) << 17) | (static_cast<uint32_t>(kGemmBM >> 4) << 24);
+
+// Byte offset of element (row, col) (col < 64) in a 128-row K-major operand
+// tile with 128-byte rows and the 128B swizzle (16-byte chunk index XOR row % 8).
+__host__ __device__ inline uint32_t sw128_offset(uint32_t row, uint32_t col) {
+    return (row >> 3) * 1024u + (row & 7u) * 128u + ((((col >> 3) ^ (row & 7u)) & 7u) << 4) + (col & 7u) * 2u;
+}
+
+__device__ __forceinline__ void split_f16(float w, __half& hi, __half& lo) {
+    hi = __float2half_rn(w);
+    lo = __float2half_rn(__fsub_rn(w, __half2float(hi)));
+}
+
+// Dequantise one K half (64 columns) of a raw stage (8 Q8T tiles = 128 rows x
+// 128 columns) into w_hi / w_lo.  t = 0..127: thread t handles Q8T tile t/16
+// and one of the 16 lanes whose 32-column blocks fall into half h.
+__device__ __forceinline__ void dequant_half(const uint8_t* raw, int t, int h, uint8_t* whi, uint8_t* wlo) {
+    const int tile = t >> 4, i = t & 15;
+    const int ln = 4 * (i >> 1) + 2 * h + (i & 1);  // Q8T lane: rows 2*(ln/4)+{0,1}, block ln % 4
+    const uint8_t* src = raw + tile * kTileBytes;
+    const uint32_t sw = *reinterpret_cast<const uint32_t*>(src + kTileQBytes + 4 * ln);
+    const float s_even = half_bits_to_float(sw & 0xffffu), s_odd = half_bits_to_float(sw >> 16);
+    const int kb = 32 * ((ln & 3) - 2 * h);  // 0 or 32 within the half
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const uint4 q = *reinterpret_cast<const uint4*>(src + (s * 32 + ln) * 16);
+        const uint32_t row = tile * 16 + 2 * (ln >> 2) + (s >> 1);
+        const uint32_t k0 = kb + 16 * (s & 1);
+        const float sc = (s >> 1) ? s_odd : s_even;
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {  // two 16-byte chunks of 8 halves
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t word = qw[c * 2 + e / 2];
+                const int sh = 16 * (e & 1);
+                const float w0 = __fmul_rn(static_cast<float>(static_cast<int8_t>((word >> sh) & 0xffu)), sc);
+                const float w1 = __fmul_rn(static_cast<float>(static_cast<int8_t>((word >> (sh + 8)) & 0xffu)), sc);
+                __half h0, l0, h1, l1;
+                split_f16(w0, h0, l0);
+                split_f16(w1, h1, l1);
+                hw[e] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+                lw[e] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+            }
+            const uint32_t off = sw128_offset(row, k0 + 8 * c);
+            *reinterpret_cast<uint4*>(whi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(wlo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    q8t_gemm_kernel(const __grid_constant__ TmaMap x_hi, const __grid_constant__ TmaMap x_lo, const GemmParams p) {
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = sm;
+    uint8_t* raw = sm + kGemmStages * kGemmStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(raw + kGemmRawStages * kGemmRawBytes);
+    uint64_t* empty = full + kGemmStages;
+    uint64_t* raw_full = empty + kGemmStages;
+    uint64_t* raw_empty = raw_full + kGemmRawStages;
+    uint64_t* acc_full = raw_empty + kGemmRawStages;  // [2]: chunk accumulator ready
+    uint64_t* acc_empty = acc_full + 2;               // [2]: chunk accumulator drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t n0 = blockIdx.x * kGemmBN, m0 = blockIdx.y * kGemmBM;
+    const uint32_t KT = p.k / kTileCols;  // raw stages (128 K columns each)
+    const uint32_t NI = 2 * KT;           // operand stages (64 K columns each)
+    const uint32_t NC = (NI + kGemmChunkStages - 1) / kGemmChunkStages;  // accumulator chunks
+
+    if (tid == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(&full[s], 1 + 4);
+            mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < kGemmRawStages; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], 4);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 8);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * kGemmBN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint8_t* wg = p.w + static_cast<uint64_t>(n0 / kTileRows) * KT * kTileBytes;
+            for (uint32_t kt = 0; kt < KT; ++kt) {
+                const uint32_t r = kt % kGemmRawStages;
+                if (kt >= kGemmRawStages) ok &= mbar_wait_bounded(&raw_empty[r], ((kt / kGemmRawStages) - 1) & 1);
+                mbar_arrive_expect_tx(&raw_full[r], kGemmRawBytes);
+                for (int g = 0; g < kGemmBN / kTileRows; ++g) {
+                    bulk_copy_g2s(raw + r * kGemmRawBytes + g * kTileBytes,
+                                  wg + (static_cast<uint64_t>(g) * KT + kt) * kTileBytes, kTileBytes, &raw_full[r]);
+                }
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t i = 2 * kt + h, s = i % kGemmStages;
+                    if (i >= kGemmStages) ok &= mbar_wait_bounded(&empty[s], ((i / kGemmStages) - 1) & 1);
+                    uint8_t* st = ring + s * kGemmStageBytes;
+                    mbar_arrive_expect_tx(&full[s], 2 * kGemmOpTile);
+                    const int kx = static_cast<int>(kt * kTileCols + h * kGemmBK);
+                    tma_load_2d(st, &x_hi, kx, static_cast<int>(m0), &full[s]);
+                    tma_load_2d(st + kGemmOpTile, &x_lo, kx, static_cast<int>(m0), &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            for (uint32_t i = 0; i < NI; ++i) {
+                const uint32_t c = i / kGemmChunkStages, a = c & 1, first = i % kGemmChunkStages == 0;
+                if (first && c >= 2) ok &= mbar_wait_bounded(&acc_empty[a], ((c / 2) - 1) & 1);
+                const uint32_t s = i % kGemmStages;
+                ok &= mbar_wait_bounded(&full[s], (i / kGemmStages) & 1);
+                tc_fence_after();
+                const uint32_t base = smem_addr(ring + s * kGemmStageBytes);
+                const uint32_t acc = tmem + a * kGemmBN;
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint32_t o = kk * 32;  // 16 fp16 = 32 bytes along K inside the swizzle atom
+                    const uint64_t ahi = sw128_desc(base + o), alo = sw128_desc(base + kGemmOpTile + o);
+                    const uint64_t bhi = sw128_desc(base + 2 * kGemmOpTile + o), blo = sw128_desc(base + 3 * kGemmOpTile + o);
+                    umma_f16(acc, ahi, bhi, kGemmIdesc, (first && kk == 0) ? 0u : 1u);
+                    umma_f16(acc, alo, bhi, kGemmIdesc, 1u);
+                    umma_f16(acc, ahi, blo, kGemmIdesc, 1u);
+                }
+                umma_commit(&empty[s]);
+                if ((i + 1) % kGemmChunkStages == 0 || i + 1 == NI) umma_commit(&acc_full[a]);
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------------------------------- dequant
+        const int t = tid - 64;  // 0..127
+        for (uint32_t kt = 0; kt < KT; ++kt) {
+            const uint32_t r = kt % kGemmRawStages;
+            ok &= mbar_wait_bounded(&raw_full[r], (kt / kGemmRawStages) & 1);
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t i = 2 * kt + h, s = i % kGemmStages;
+                if (i >= kGemmStages) ok &= mbar_wait_bounded(&empty[s], ((i / kGemmStages) - 1) & 1);
+                uint8_t* st = ring + s * kGemmStageBytes;
+                dequant_half(raw + r * kGemmRawBytes, t, h, st + 2 * kGemmOpTile, st + 3 * kGemmOpTile);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[r]);
+        }
+    } else {
+        // ------------------------------------------------------- epilogue
+        const uint32_t q = warp & 3;  // TMEM lane quarter this warp may access
+        const uint32_t cb = ((warp - 6) >> 2) * kGemmEpiCols;  // first accumulator column of this warp
+        const uint32_t row = m0 + 32 * q + lane;
+        float sum[kGemmEpiCols];
+#pragma unroll
+        for (int j = 0; j < kGemmEpiCols; ++j) sum[j] = 0.0f;
+        for (uint32_t c = 0; c < NC; ++c) {
+            const uint32_t a = c & 1;
+            ok &= mbar_wait_bounded(&acc_full[a], (c / 2) & 1);
+            tc_fence_after();
+#pragma unroll
+            for (int c0 = 0; c0 < kGemmEpiCols; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((32 * q) << 16) + a * kGemmBN + cb + c0, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum[c0 + j] = __fadd_rn(sum[c0 + j], __uint_as_float(v[j]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+#pragma unroll
+        for (int cl = 0; cl < kGemmEpiCols; cl += 32) {
+            float* v = sum + cl;
+            const uint32_t c0 = cb + cl;
+            if (row >= p.m) continue;
+            if (EPI == kGemmStore) {
+                float4* dst = reinterpret_cast<float4*>(p.y + static_cast<uint64_t>(row) * p.ldy + n0 + c0);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+                }
+            } else {
+                // columns c0..c0+31 = two row groups of 8 gate + 8 up rows
+                const uint64_t o = static_cast<uint64_t>(row) * p.ld_act + (n0 + c0) / 2;
+                uint32_t hw[8], lw[8];
+                float a[16];
+#pragma unroll
+                for (int gg = 0; gg < 2; ++gg) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        a[8 * gg + j] = __fmul_rn(gelu_tanh(v[16 * gg + j]), v[16 * gg + 8 + j]);
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    __half h0, l0, h1, l1;
+                    split_f16(a[2 * e], h0, l0);
+                    split_f16(a[2 * e + 1], h1, l1);
+                    hw[e] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+                    lw[e] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+                }
+                uint4* dh = reinterpret_cast<uint4*>(p.act_hi + o);
+                uint4* dl = reinterpret_cast<uint4*>(p.act_lo + o);
+                dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+                if (p.act_f32) {
+                    float4* df = reinterpret_cast<float4*>(p.act_f32 + o);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) df[e] = make_float4(a[4 * e], a[4 * e + 1], a[4 * e + 2], a[4 * e + 3]);
+                }
+            }
+        }
+    }
+    __syncwarp();  // reconverge each warp (lane 0 of warps 0 and 1 ran alone) before the CTA barrier
+    if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * kGemmBN);
+    }
+}
+
+}  // namespace vrt

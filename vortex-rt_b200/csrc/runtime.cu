@@ -231,6 +231,7 @@ int vrt_ctx_destroy(vrt_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     for (auto& kv : ctx->allocs) cudaFree(kv.first);
     cudaFree(ctx->d_key);
+    cudaFree(ctx->ws);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return VRT_OK;

@@ -16,6 +16,8 @@ struct vrt_ctx {
     cudaStream_t stream = nullptr;
     cudaDeviceProp prop{};
     unsigned long long* d_key = nullptr;  // argmax scratch
+    void* ws = nullptr;                   // tensor-core GEMM operand scratch, grown on demand
+    size_t ws_bytes = 0;
     std::mutex mu;
     std::unordered_map<void*, size_t> allocs;
 };

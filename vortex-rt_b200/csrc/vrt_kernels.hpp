@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include "attention.cuh"
+#include "gemm_q8t.cuh"
 #include "gemv_q8t.cuh"
 
 namespace vrt {
@@ -14,6 +15,12 @@ uint32_t gemv_smem_bytes(int pro, uint32_t cols);
 cudaError_t gemv_init_attributes();
 cudaError_t argmax_unkey_launch(const unsigned long long* key, uint32_t* out, cudaStream_t s);
 cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl);
+
+// Tensor-core Q8T GEMM (gemm.cu): epilogue `epi` (GemmEpi); operands from
+// make_f16_tmap over fp16 hi / lo activation matrices of at least p.m rows.
+cudaError_t gemm_q8t(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s);
+int make_f16_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols);
+cudaError_t split_f16(const float* x, uint64_t n, __half* hi, __half* lo, cudaStream_t s);
 
 // CTAs for a Q8T mat-vec: one per SM, at most one per row group.
 inline int gemv_grid(int sms, uint32_t rows) {

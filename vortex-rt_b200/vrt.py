@@ -100,6 +100,8 @@ _SIGS = {
     "vrt_q8t_gate_up": (_i, [_vp, _vp, _u32, _u32, _vp, _vp, _vp]),
     "vrt_q8t_ffn": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp]),
     "vrt_q8t_lm_head_argmax": (_i, [_vp, _vp, _u32, _u32, _vp, _vp, _vp, _vp]),
+    "vrt_q8t_gemm": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
+    "vrt_q8t_gemm_gelu": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
     "vrt_model_options_default": (None, [C.POINTER(ModelOptions)]),
     "vrt_model_load": (_i, [_vp, C.c_char_p, C.POINTER(ModelOptions), C.POINTER(_vp)]),
     "vrt_model_create_synthetic": (_i, [_vp, C.POINTER(Gemma3Config), _u64, C.POINTER(ModelOptions),
