@@ -203,6 +203,9 @@ typedef struct {
     int use_pdl;            /* programmatic dependent launch between kernels    */
     int tp_exchange;        /* VRT_TP_PEER (default) or VRT_TP_NCCL             */
     uint32_t tp_wait_ms;    /* bound of one wait on a peer; 0 = 10000 ms        */
+    uint32_t prefill_chunk; /* prompt tokens per batched (tensor-core) prefill
+                               pass; 0 = 2048; 1 = token by token through the
+                               decode step, the reference's method            */
 } vrt_model_options;
 
 /* How the partial sums of the row-parallel projections (attention output,
@@ -216,7 +219,9 @@ typedef struct {
 enum { VRT_TP_PEER = 0, VRT_TP_NCCL = 1 };
 
 /* Defaults: max_positions 0, single GPU, use_graph = 1, use_pdl = 1,
- * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0. */
+ * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0, prefill_chunk = 0.  Batched
+ * prefill runs on one GPU (tp_world <= 1) without tracing; otherwise prompts
+ * go token by token. */
 VRT_API void vrt_model_options_default(vrt_model_options* o);
 
 /* Load a Gemma 3 Q8_0 GGUF: weights repacked into the device arena, norms,

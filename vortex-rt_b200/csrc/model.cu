@@ -36,6 +36,7 @@
 #include <string>
 #include <vector>
 
+#include "prefill.cuh"
 #include "vortexrt/gguf.hpp"
 #include "vrt_device.cuh"
 #include "vrt_internal.hpp"
@@ -305,6 +306,15 @@ struct vrt_model {
     unsigned long long** tp_peers_dev = nullptr;        // the same table on the device
     float* tp_sum = nullptr;                            // reduced vectors, [2][d]
     uint32_t* tp_bar = nullptr;                         // grid barrier counter, generation
+    // batched prefill buffers, [chunk][...] rows (allocated at the first batched prefill)
+    struct Prefill {
+        uint32_t cap = 0;
+        void* mem = nullptr;
+        float *h0 = nullptr, *h1 = nullptr, *qkv = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr,
+              *dn = nullptr;
+        __half *xh = nullptr, *xl = nullptr, *ah = nullptr, *al = nullptr;
+        vrt::TmaMap xd_hi, xd_lo, xq_hi, xq_lo, xf_hi, xf_lo;  // operands with K = d, q width, ffn width
+    } pf;
 };
 
 namespace vrt {
@@ -1078,6 +1088,7 @@ static void destroy_model(vrt_model* m) {
     cudaFree(m->prompt);
     cudaFree(m->st);
     cudaFree(m->key_tmp);
+    cudaFree(m->pf.mem);
     if (m->st_host) cudaFreeHost(m->st_host);
     if (m->hidden_host) cudaFreeHost(m->hidden_host);
     delete m;
@@ -1099,6 +1110,205 @@ static int begin_model(vrt_ctx* ctx, const vrt_model_options* opts, vrt_model** 
     }
     VRT_CUDA(cudaSetDevice(ctx->device));
     VRT_CUDA(gemv_init_attributes());
+    return VRT_OK;
+}
+
+// ------------------------------------------------------- batched prefill
+
+static int prefill_alloc(vrt_model* m, uint32_t cap) {
+    auto& B = m->pf;
+    if (B.cap >= cap) return VRT_OK;
+    if (B.mem) {
+        VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+        cudaFree(B.mem);
+        B = vrt_model::Prefill{};
+    }
+    const auto& c = m->cfg;
+    const uint64_t d = c.embedding_length, hd = c.head_dim, C = cap;
+    const uint64_t xw = std::max<uint64_t>(d, m->qwl);
+    const uint64_t f32[] = {C * d, C * d, C * (m->qwl + 2ull * m->kwl), C * m->Hl * hd, C * m->KVl * hd,
+                            C * m->KVl * hd, C * d, C * d};
+    const uint64_t f16[] = {C * xw, C * xw, C * m->ffl, C * m->ffl};
+    uint64_t total = 0;
+    for (auto n : f32) total += align256(n * 4);
+    for (auto n : f16) total += align256(n * 2);
+    VRT_CUDA(cudaMalloc(&B.mem, total));
+    uint8_t* p = static_cast<uint8_t*>(B.mem);
+    float** fd[] = {&B.h0, &B.h1, &B.qkv, &B.q, &B.k, &B.v, &B.o, &B.dn};
+    for (int i = 0; i < 8; ++i) {
+        *fd[i] = reinterpret_cast<float*>(p);
+        p += align256(f32[i] * 4);
+    }
+    __half** hd16[] = {&B.xh, &B.xl, &B.ah, &B.al};
+    for (int i = 0; i < 4; ++i) {
+        *hd16[i] = reinterpret_cast<__half*>(p);
+        p += align256(f16[i] * 2);
+    }
+    VRT_CUDA(cudaMemsetAsync(B.mem, 0, total, m->ctx->stream));
+    VRT_TRY(make_f16_tmap(&B.xd_hi, B.xh, C, d));
+    VRT_TRY(make_f16_tmap(&B.xd_lo, B.xl, C, d));
+    VRT_TRY(make_f16_tmap(&B.xq_hi, B.xh, C, m->qwl));
+    VRT_TRY(make_f16_tmap(&B.xq_lo, B.xl, C, m->qwl));
+    VRT_TRY(make_f16_tmap(&B.xf_hi, B.ah, C, m->ffl));
+    VRT_TRY(make_f16_tmap(&B.xf_lo, B.al, C, m->ffl));
+    B.cap = cap;
+    return VRT_OK;
+}
+
+template <int HD, int G>
+static cudaError_t prefill_attn_launch_t(const PrefillAttnParams& a, cudaStream_t s) {
+    static uint64_t done = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    constexpr uint32_t smem = prefill_attn_smem<HD>();
+    if (dev < 64 && !(done & (1ull << dev))) {
+        e = cudaFuncSetAttribute(prefill_attention_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        done |= 1ull << dev;
+    }
+    constexpr uint32_t QB = kPaRows / G;
+    const dim3 grid((a.n + QB - 1) / QB, a.KV);
+    prefill_attention_kernel<HD, G><<<grid, kPaThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <int HD>
+static cudaError_t prefill_attn_launch_hd(const PrefillAttnParams& a, uint32_t G, cudaStream_t s) {
+    switch (G) {
+    case 1: return prefill_attn_launch_t<HD, 1>(a, s);
+    case 2: return prefill_attn_launch_t<HD, 2>(a, s);
+    case 4: return prefill_attn_launch_t<HD, 4>(a, s);
+    case 8: return prefill_attn_launch_t<HD, 8>(a, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+static cudaError_t prefill_attn_launch(const PrefillAttnParams& a, uint32_t hd, uint32_t G, cudaStream_t s) {
+    switch (hd) {
+    case 64: return prefill_attn_launch_hd<64>(a, G, s);
+    case 128: return prefill_attn_launch_hd<128>(a, G, s);
+    case 256: return prefill_attn_launch_hd<256>(a, G, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+static cudaError_t qk_rope_launch(const float* qkv, vrt_model* m, const LayerW& L, uint32_t p0, uint32_t n, float* q,
+                                  float* k, float* v, cudaStream_t s) {
+    const auto& c = m->cfg;
+    auto F = [&](uint64_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+    const float* cs = L.global ? m->rope_cos_g : m->rope_cos_l;
+    const float* sn = L.global ? m->rope_sin_g : m->rope_sin_l;
+    switch (c.head_dim) {
+    case 64: qk_rope_rows_kernel<2><<<n, 256, 0, s>>>(qkv, m->Hl, m->KVl, F(L.n_q), F(L.n_k), cs, sn, p0, c.rms_epsilon, q, k, v); break;
+    case 128: qk_rope_rows_kernel<4><<<n, 256, 0, s>>>(qkv, m->Hl, m->KVl, F(L.n_q), F(L.n_k), cs, sn, p0, c.rms_epsilon, q, k, v); break;
+    case 256: qk_rope_rows_kernel<8><<<n, 256, 0, s>>>(qkv, m->Hl, m->KVl, F(L.n_q), F(L.n_k), cs, sn, p0, c.rms_epsilon, q, k, v); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+// Shapes the tensor-core GEMM tiles (128-row weight tiles) and the prefill
+// attention is instantiated for (query heads per KV head 1, 2, 4 or 8).
+static bool prefill_supported(const vrt_model* m) {
+    const uint32_t d = m->cfg.embedding_length, G = m->KVl ? m->Hl / m->KVl : 0;
+    return (m->qwl + 2 * m->kwl) % kGemmBN == 0 && d % kGemmBN == 0 && m->qwl % kTileCols == 0 &&
+           (2 * m->ffl) % kGemmBN == 0 && m->ffl % kTileCols == 0 && (G == 1 || G == 2 || G == 4 || G == 8);
+}
+
+// The prompt (already in m->prompt, n tokens) through every layer in chunks
+// of pf.cap tokens, then the fused LM head + argmax on the last token and the
+// decode finalize: the step state ends exactly as after a token-by-token
+// prefill (position n, first generated id emitted).
+static int prefill_batched(vrt_model* m, uint32_t n) {
+    const auto& c = m->cfg;
+    const uint32_t want = m->opt.prefill_chunk ? m->opt.prefill_chunk : 2048u;
+    VRT_TRY(prefill_alloc(m, std::min(want, m->P)));
+    auto& B = m->pf;
+    cudaStream_t s = m->ctx->stream;
+    const uint32_t d = c.embedding_length, hd = c.head_dim, G = m->Hl / m->KVl;
+    uint32_t* status = &m->st->status;
+    auto F = [&](uint64_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+    auto gemm = [&](int epi, const TmaMap& hi, const TmaMap& lo, const uint8_t* w, uint32_t rows, uint32_t k,
+                    uint32_t mrows, float* y, __half* ah, __half* al) -> int {
+        GemmParams p{};
+        p.w = w;
+        p.n = rows;
+        p.k = k;
+        p.m = mrows;
+        p.status = status;
+        p.y = y;
+        p.ldy = rows;
+        p.act_hi = ah;
+        p.act_lo = al;
+        p.ld_act = rows / 2;
+        VRT_CUDA(gemm_q8t(epi, hi, lo, p, s));
+        return VRT_OK;
+    };
+    uint32_t last = 0;
+    for (uint32_t p0 = 0; p0 < n; p0 += B.cap) {
+        const uint32_t nc = std::min(B.cap, n - p0);
+        last = nc;
+        embed_rows_kernel<<<nc, kRowThreads, 0, s>>>(m->arena + m->embd, m->prompt + p0, c.vocab_size, d,
+                                                    std::sqrt(static_cast<float>(d)), F(m->layers[0].n_attn),
+                                                    c.rms_epsilon, B.h0, B.xh, B.xl, status);
+        VRT_CUDA(cudaGetLastError());
+        for (uint32_t l = 0; l < c.block_count; ++l) {
+            const auto& L = m->layers[l];
+            if (l > 0) {
+                resid_rows_kernel<<<nc, kRowThreads, 0, s>>>(B.dn, B.h1, F(m->layers[l - 1].n_post_ffw), F(L.n_attn),
+                                                            c.rms_epsilon, d, B.h0, B.xh, B.xl, status);
+                VRT_CUDA(cudaGetLastError());
+            }
+            VRT_TRY(gemm(kGemmStore, B.xd_hi, B.xd_lo, m->arena + L.qkv, m->qwl + 2 * m->kwl, d, nc, B.qkv, nullptr,
+                         nullptr));
+            VRT_CUDA(qk_rope_launch(B.qkv, m, L, p0, nc, B.q, B.k, B.v, s));
+            PrefillAttnParams a{};
+            a.q = B.q;
+            a.k = B.k;
+            a.v = B.v;
+            a.k_cache = L.k_cache;
+            a.v_cache = L.v_cache;
+            a.cap = L.cap;
+            a.window = L.global ? 0u : c.sliding_window;
+            a.p0 = p0;
+            a.n = nc;
+            a.H = m->Hl;
+            a.KV = m->KVl;
+            a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+            a.out_hi = B.xh;
+            a.out_lo = B.xl;
+            VRT_CUDA(prefill_attn_launch(a, hd, G, s));
+            kv_store_kernel<<<dim3(nc, m->KVl), 128, 0, s>>>(B.k, B.v, L.k_cache, L.v_cache, L.cap, m->KVl, hd, p0, nc);
+            VRT_CUDA(cudaGetLastError());
+            VRT_TRY(gemm(kGemmStore, B.xq_hi, B.xq_lo, m->arena + L.o, d, m->qwl, nc, B.o, nullptr, nullptr));
+            resid_rows_kernel<<<nc, kRowThreads, 0, s>>>(B.o, B.h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
+                                                        B.h1, B.xh, B.xl, status);
+            VRT_CUDA(cudaGetLastError());
+            VRT_TRY(gemm(kGemmGeluSplit, B.xd_hi, B.xd_lo, m->arena + L.gu, 2 * m->ffl, d, nc, nullptr, B.ah, B.al));
+            VRT_TRY(gemm(kGemmStore, B.xf_hi, B.xf_lo, m->arena + L.down, d, m->ffl, nc, B.dn, nullptr, nullptr));
+        }
+    }
+    // last prompt token: final residual + output norm -> tied LM head + argmax
+    const auto& lastL = m->layers[c.block_count - 1];
+    GemvParams p{};
+    const uint32_t kt = d / kTileCols;
+    p.w = m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes;
+    p.rows = m->vocab_hi - m->vocab_lo;
+    p.cols = d;
+    p.x = B.dn + static_cast<uint64_t>(last - 1) * d;
+    p.h_prev = B.h1 + static_cast<uint64_t>(last - 1) * d;
+    p.w_post = F(lastL.n_post_ffw);
+    p.w_pre = F(m->out_norm);
+    p.h_out = m->hidden;
+    p.y = m->logits;
+    p.amax = &m->st->key;
+    p.row_base = m->vocab_lo;
+    p.status = status;
+    p.eps = c.rms_epsilon;
+    VRT_CUDA(gemv_q8t(kProResidFinal, kEpiArgmax, p, gemv_grid(m->ctx->prop.multiProcessorCount, p.rows), s, false));
+    VRT_CUDA(launch(finalize_decode_kernel, dim3(1), dim3(1), 0, s, false, m->st, c.vocab_size, m->out_ids, kMaxSteps,
+                    TpParams{}));
     return VRT_OK;
 }
 
@@ -1288,11 +1498,17 @@ int vrt_prefill(vrt_model* m, const uint32_t* h_prompt, uint32_t n) {
     VRT_CUDA(cudaMemcpyAsync(m->prompt, h_prompt, 4ull * n, cudaMemcpyHostToDevice, s));
     StepState* sh = m->st_host;
     memset(sh, 0, kStepStateHostBytes);
-    sh->token = h_prompt[0];
+    const bool batched = m->world <= 1 && !m->trace_on && m->opt.prefill_chunk != 1 && n >= 2 && prefill_supported(m);
+    sh->token = batched ? h_prompt[n - 1] : h_prompt[0];
+    sh->pos = batched ? n - 1 : 0;  // the batched pass leaves only the last token's LM head + finalize
     sh->prompt_count = n;
     VRT_CUDA(cudaMemcpyAsync(m->st, sh, kStepStateHostBytes, cudaMemcpyHostToDevice, s));
-    for (uint32_t i = 0; i + 1 < n; ++i) VRT_TRY(run_step(m, false));
-    VRT_TRY(run_step(m, true));
+    if (batched) {
+        VRT_TRY(prefill_batched(m, n));
+    } else {
+        for (uint32_t i = 0; i + 1 < n; ++i) VRT_TRY(run_step(m, false));
+        VRT_TRY(run_step(m, true));
+    }
     VRT_CUDA(cudaMemcpyAsync(sh, m->st, sizeof(StepState), cudaMemcpyDeviceToHost, s));
     VRT_CUDA(cudaStreamSynchronize(s));
     uint32_t status;
