@@ -3,8 +3,11 @@
 Default workload: the 27B-shaped decoder (vocab
 262144, d 5376, 62 layers, 32 q / 16 KV heads of 128, ffn 21504, window 1024,
 5:1 local:global) with seeded synthetic Q8_0 weights generated on the device,
-a 2048-token seeded prompt prefilled token by token, then greedy decode.
-`--workload 270m` runs config 0's 270M shape instead.
+a 2048-token seeded prompt prefilled in one batched pass on the tensor cores
+(tcgen05 GEMMs; token by token under tensor parallelism), then greedy decode.
+`--workload 270m` runs config 0's 270M shape (8-token prompt) instead, and
+`--workload 270m-long` config 2 (270M, 4096-token prompt, decode past the
+512-token window).
 
 One step = one decoded token (batch 1).  Under torchrun (N > 1) the model is
 tensor-parallel over N GPUs (Q/K/V, gate, up column-sharded; o-proj, down
@@ -23,6 +26,7 @@ Printed JSON line:
   cpu_baseline   the CPU oracle (C restatement of the reference token loop,
                  GQA-generalised; the reference itself refuses head_count_kv != 1)
                  on a bounded sample, extrapolated to one token
+  prefill        the prompt's prefill, device-timed (CUDA events), tokens/s
   clocks         nvidia-smi samples taken during the timed region
 """
 
@@ -44,7 +48,7 @@ sys.path[:0] = [os.path.join(ROOT, "vortex-rt_b200"), os.path.join(ROOT, "oracle
 
 import synth_gguf as sg  # noqa: E402
 
-PROMPT_LEN = {"27b": 2048, "270m": 8}
+PROMPT_LEN = {"27b": 2048, "270m": 8, "270m-long": 4096}
 METRIC = "decode tok/s (Gemma3-shaped Q8_0, bs=1 greedy)"
 
 
@@ -132,7 +136,7 @@ def cpu_baseline(workload: str, threads: int) -> dict:
     import oracle as O
 
     shape = shape_for(workload)
-    if workload == "270m":
+    if workload != "27b":
         sample_layers, sample_vocab = shape.block_count, shape.vocab_size
     else:
         sample_layers, sample_vocab = 2, 16384
@@ -191,7 +195,7 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="27b", choices=["27b", "270m"])
+    ap.add_argument("--workload", default="27b", choices=["27b", "270m", "270m-long"])
     ap.add_argument("--prompt-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
@@ -242,12 +246,21 @@ def main():
         if dist_on:
             dist.barrier()
 
-    # prefill (token by token through the decode step, as the reference does)
-    t_pf = time.perf_counter()
-    m.prefill(prompt)
-    t_pf = time.perf_counter() - t_pf
-
+    # prefill: one batched tensor-core pass on a single GPU, token by token under TP
     stream = torch.cuda.ExternalStream(ctx.stream)
+    pf0 = torch.cuda.Event(enable_timing=True)
+    pf1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    pf0.record(stream)
+    m.prefill(prompt)
+    pf1.record(stream)
+    ctx.sync()
+    t_pf = pf0.elapsed_time(pf1) / 1000.0
+    tpf = torch.tensor([t_pf], dtype=torch.float64, device="cuda")
+    if dist_on:
+        dist.all_reduce(tpf, op=dist.ReduceOp.MAX)
+    t_pf = float(tpf.item())
+
     # warmup
     m.decode_steps_async(args.warmup)
     ctx.sync()
@@ -303,10 +316,13 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "q8_0*f32",
             "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
-            "config": {"workload": f"config 4: {args.workload}-shaped Gemma 3 Q8_0, bs=1 greedy decode after a "
-                                   f"{prompt_len}-token prefill" if args.workload == "27b" else
-                                   f"config 0: 270M-shaped Gemma 3 Q8_0, bs=1 greedy decode after {prompt_len} "
-                                   "prompt tokens",
+            "config": {"workload": {"27b": f"config 4: 27B-shaped Gemma 3 Q8_0, bs=1 greedy decode after a "
+                                           f"{prompt_len}-token prefill",
+                                    "270m": f"config 0: 270M-shaped Gemma 3 Q8_0, bs=1 greedy decode after "
+                                            f"{prompt_len} prompt tokens",
+                                    "270m-long": f"config 2: 270M-shaped Gemma 3 Q8_0, {prompt_len}-token batched "
+                                                 "prefill, then bs=1 greedy decode past the 512-token window"
+                                    }[args.workload],
                        "d_model": shape.embedding_length, "layers": shape.block_count,
                        "heads": f"{shape.head_count}q/{shape.head_count_kv}kv x {shape.head_dim}",
                        "ffn": shape.feed_forward_length, "vocab": shape.vocab_size, "global_batch": 1,
@@ -325,7 +341,9 @@ def main():
                          "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": k_bytes,
                          "ms_per_launch": k_ms, "traffic": tr},
             "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 40},
-            "prefill_s": t_pf,
+            "prefill": {"tokens": prompt_len, "s": t_pf, "tok_s": prompt_len / t_pf,
+                        "method": "token by token (tensor parallel)" if world > 1 else
+                                  "batched: tcgen05 Q8_0 GEMMs + tiled prefill attention, chunks of 2048"},
             "device_status": status,
             "clocks": clocks,
         }

@@ -150,34 +150,39 @@ __device__ __forceinline__ void split_f16(float w, __half& hi, __half& lo) {
 // Dequantise one K half (64 columns) of a raw stage (8 Q8T tiles = 128 rows x
 // 128 columns) into w_hi / w_lo.  t = 0..127: thread t handles Q8T tile t/16
 // and one of the 16 lanes whose 32-column blocks fall into half h.
+// Packed fp16 arithmetic, two weights per instruction: a byte permute puts
+// each int8 (offset by 128) under the fp16 exponent of 1024, so subtracting
+// 1152 gives q exactly; hi = RN(q * s) (one HMUL2 of the exact product) and
+// lo = RN(q * s - hi) (one HFMA2) -- bit-identical to computing w = q * s in
+// fp32 (exact) and splitting it there.
 __device__ __forceinline__ void dequant_half(const uint8_t* raw, int t, int h, uint8_t* whi, uint8_t* wlo) {
     const int tile = t >> 4, i = t & 15;
     const int ln = 4 * (i >> 1) + 2 * h + (i & 1);  // Q8T lane: rows 2*(ln/4)+{0,1}, block ln % 4
     const uint8_t* src = raw + tile * kTileBytes;
     const uint32_t sw = *reinterpret_cast<const uint32_t*>(src + kTileQBytes + 4 * ln);
-    const float s_even = half_bits_to_float(sw & 0xffffu), s_odd = half_bits_to_float(sw >> 16);
+    const __half2 s_even = __half2half2(__ushort_as_half(static_cast<unsigned short>(sw & 0xffffu)));
+    const __half2 s_odd = __half2half2(__ushort_as_half(static_cast<unsigned short>(sw >> 16)));
+    const __half2 bias = __float2half2_rn(1152.0f);
     const int kb = 32 * ((ln & 3) - 2 * h);  // 0 or 32 within the half
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const uint4 q = *reinterpret_cast<const uint4*>(src + (s * 32 + ln) * 16);
         const uint32_t row = tile * 16 + 2 * (ln >> 2) + (s >> 1);
         const uint32_t k0 = kb + 16 * (s & 1);
-        const float sc = (s >> 1) ? s_odd : s_even;
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        const __half2 sc = (s >> 1) ? s_odd : s_even;
+        const uint32_t qw[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {  // two 16-byte chunks of 8 halves
             uint32_t hw[4], lw[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const uint32_t word = qw[c * 2 + e / 2];
-                const int sh = 16 * (e & 1);
-                const float w0 = __fmul_rn(static_cast<float>(static_cast<int8_t>((word >> sh) & 0xffu)), sc);
-                const float w1 = __fmul_rn(static_cast<float>(static_cast<int8_t>((word >> (sh + 8)) & 0xffu)), sc);
-                __half h0, l0, h1, l1;
-                split_f16(w0, h0, l0);
-                split_f16(w1, h1, l1);
-                hw[e] = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
-                lw[e] = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+                const uint32_t biased = __byte_perm(word, 0x64646464u, (e & 1) ? 0x4342u : 0x4140u);
+                const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&biased), bias);
+                const __half2 hi = __hmul2(qv, sc);
+                const __half2 lo = __hfma2(qv, sc, __hneg2(hi));
+                hw[e] = *reinterpret_cast<const uint32_t*>(&hi);
+                lw[e] = *reinterpret_cast<const uint32_t*>(&lo);
             }
             const uint32_t off = sw128_offset(row, k0 + 8 * c);
             *reinterpret_cast<uint4*>(whi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
