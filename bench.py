@@ -7,7 +7,11 @@ a 2048-token seeded prompt prefilled in one batched pass on the tensor cores
 (tcgen05 GEMMs; token by token under tensor parallelism), then greedy decode.
 `--workload 270m` runs config 0's 270M shape (8-token prompt) instead, and
 `--workload 270m-long` config 2 (270M, 4096-token prompt, decode past the
-512-token window).
+512-token window).  Batched decode of independent sequences (tensor-core
+GEMMs with M = sequences, per-sequence KV caches): `--workload 270m-batch`
+is config 3 (256 sequences x 1024-token prompts, split evenly over the N
+ranks as replicas with no collective), `--workload 27b-bs32` config 4 at
+batch 32 on one GPU.
 
 One step = one decoded token (batch 1).  Under torchrun (N > 1) the model is
 tensor-parallel over N GPUs (Q/K/V, gate, up column-sharded; o-proj, down
@@ -48,7 +52,8 @@ sys.path[:0] = [os.path.join(ROOT, "vortex-rt_b200"), os.path.join(ROOT, "oracle
 
 import synth_gguf as sg  # noqa: E402
 
-PROMPT_LEN = {"27b": 2048, "270m": 8, "270m-long": 4096}
+PROMPT_LEN = {"27b": 2048, "270m": 8, "270m-long": 4096, "270m-batch": 1024, "27b-bs32": 2048}
+BATCH_SEQS = {"270m-batch": 256, "27b-bs32": 32}
 METRIC = "decode tok/s (Gemma3-shaped Q8_0, bs=1 greedy)"
 
 
@@ -113,7 +118,7 @@ class ClockSampler:
 
 
 def shape_for(workload: str) -> sg.Gemma3Shape:
-    return sg.SHAPES["27b" if workload == "27b" else "270m"]
+    return sg.SHAPES["27b" if workload.startswith("27b") else "270m"]
 
 
 def bytes_per_token(shape: sg.Gemma3Shape, pos: int) -> int:
@@ -136,7 +141,7 @@ def cpu_baseline(workload: str, threads: int) -> dict:
     import oracle as O
 
     shape = shape_for(workload)
-    if workload != "27b":
+    if not workload.startswith("27b"):
         sample_layers, sample_vocab = shape.block_count, shape.vocab_size
     else:
         sample_layers, sample_vocab = 2, 16384
@@ -189,13 +194,137 @@ def run_reference_arm(args, rank: int, world: int):
     }), flush=True)
 
 
+def run_batched(args, rank: int, world: int, local: int):
+    """Configs 3 / 4-bs32: independent sequences decoded together (vrt_batch).
+    Under torchrun the sequences are split evenly over the ranks, each rank a
+    full replica with no collective on the data path ("replicas")."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import vrt
+
+    dist_on = world > 1
+    if dist_on:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    if args.workload == "27b-bs32" and world > 1:
+        raise SystemExit("27b-bs32 runs on one GPU (batched decode under tensor parallelism is not built)")
+    shape = shape_for(args.workload)
+    if args.layers:
+        shape = shape.with_(block_count=args.layers)
+    if args.vocab:
+        shape = shape.with_(vocab_size=args.vocab)
+    total = BATCH_SEQS[args.workload]
+    M = total // world
+    prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
+    e2e_steps = max(4, args.steps // 4)
+    P = prompt_len + args.warmup + args.steps + e2e_steps + 8
+    ctx = vrt.Context(local)
+    model = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=1234, max_positions=P)
+    b = vrt.Batch(model, M, P)
+    stream = torch.cuda.ExternalStream(ctx.stream)
+
+    def barrier():
+        if dist_on:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        if dist_on:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    rng = np.random.default_rng(3 + rank)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    barrier()
+    ev[0].record(stream)
+    for i in range(M):
+        b.prefill(i, [2] + rng.integers(3, shape.vocab_size, prompt_len - 1).tolist())
+    ev[1].record(stream)
+    ctx.sync()
+    t_pf = max_over_ranks(ev[0].elapsed_time(ev[1]) / 1000.0)
+    b.decode_steps(M, args.warmup)
+    ctx.sync()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ctx.sync()
+    barrier()
+    ev[2].record(stream)
+    b.decode_steps(M, args.steps)
+    ev[3].record(stream)
+    ctx.sync()
+    barrier()
+    clocks = sampler.stop()
+    ms = max_over_ranks(ev[2].elapsed_time(ev[3]))
+    tok_s = total * args.steps / (ms / 1000.0)
+    # e2e: the public call per step plus the read-back of every sequence's new id
+    ids = np.zeros(M, np.uint32)
+    barrier()
+    ctx.sync()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        b.decode_steps(M, 1)
+        b.last_ids(M, ids)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = total * e2e_steps / e2e_s
+    _, pos = b.read(0, 1)
+    status = model.device_status()
+    b.close()
+    model.close()
+    ctx.close()
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        mid = prompt_len + args.warmup + args.steps // 2
+        weights = bytes_per_token(shape, 0)  # weights + norms (+ one position of KV)
+        step_bytes = weights + M * (bytes_per_token(shape, mid) - weights)
+        achieved = step_bytes / (ms / 1000.0 / args.steps) / 1e9
+        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, os.cpu_count() or 1)
+        line = {
+            "metric": METRIC.replace("bs=1", f"batched, {total} sequences"), "value": tok_s, "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q8_0*fp16x2->f32",
+            "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
+            "config": {"workload": {"270m-batch": f"config 3: 270M-shaped Gemma 3 Q8_0, {total} sequences x "
+                                                  f"{prompt_len}-token prompts, greedy decode, sequences split over "
+                                                  f"{world} replica(s)",
+                                    "27b-bs32": f"config 4 at batch {total}: 27B-shaped, {prompt_len}-token prompts"
+                                    }[args.workload],
+                       "d_model": shape.embedding_length, "layers": shape.block_count, "vocab": shape.vocab_size,
+                       "global_batch": total, "sequences_per_gpu": M,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "positions": f"{prompt_len + args.warmup}..{prompt_len + args.warmup + args.steps}",
+                       "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB per step)"},
+            "gpu_launches": (7 * shape.block_count + 3) * args.steps,
+            "kernels_per_step": 7 * shape.block_count + 3,
+            "roofline": {"bound": "hbm", "kernel": "whole batched step: Q8_0 weights once + every sequence's KV",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_step": step_bytes, "traffic": None},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4 * M,
+                    "note": "tokens stay on the device; each step reads back every sequence's new id"},
+            "prefill": {"tokens": total * prompt_len, "s": t_pf, "tok_s": total * prompt_len / t_pf,
+                        "method": "batched tensor-core prefill per sequence"},
+            "final_position": pos,
+            "device_status": status,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="27b", choices=["27b", "270m", "270m-long"])
+    ap.add_argument("--workload", default="27b", choices=["27b", "270m", "270m-long", "270m-batch", "27b-bs32"])
     ap.add_argument("--prompt-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
@@ -214,6 +343,9 @@ def main():
     import torch.distributed as dist
 
     import vrt
+
+    if args.workload in BATCH_SEQS:
+        return run_batched(args, rank, world, local)
 
     dist_on = world > 1
     if dist_on:

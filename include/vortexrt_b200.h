@@ -289,6 +289,34 @@ VRT_API int vrt_model_trace(vrt_model* m, float* h_out);
 VRT_API int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, uint32_t iters,
                                   float* ms_per_launch, uint64_t* algorithmic_bytes);
 
+/* ---------------------------------------------------------- batched decode
+ * Independent sequences decoded together on one GPU (no reference
+ * counterpart: the reference decodes one sequence, src/gemma3.cpp:1462-1882).
+ * Each sequence has its own KV cache; a step decodes one greedy token for
+ * each of the first `count` sequences, with the projections and the tied LM
+ * head as tensor-core GEMMs of `count` rows.  Per sequence the results match
+ * decoding it alone within the north-star tolerance. */
+typedef struct vrt_batch vrt_batch;
+/* max_positions <= the model's positions; keep_logits != 0 keeps the last
+ * step's full logits per sequence (max_seqs * vocab floats) for checking. */
+VRT_API int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, int keep_logits,
+                             vrt_batch** out);
+VRT_API int vrt_batch_destroy(vrt_batch* b);
+/* Prefill sequence `seq` (batched tensor-core prefill into its cache); emits its
+ * first greedy id and sets its position to n. */
+VRT_API int vrt_batch_prefill(vrt_batch* b, uint32_t seq, const uint32_t* h_prompt, uint32_t n);
+/* `steps` greedy steps of sequences [0, count), queued on the model stream. */
+VRT_API int vrt_batch_decode_steps(vrt_batch* b, uint32_t count, uint32_t steps);
+/* Ids generated for `seq` so far (first min(count, cap) into h_ids), its count
+ * and next position.  Synchronises with the model stream. */
+VRT_API int vrt_batch_read(vrt_batch* b, uint32_t seq, uint32_t* h_ids, uint32_t cap, uint32_t* h_count,
+                           uint32_t* h_position);
+/* The latest generated id of each of the first `count` sequences (their next
+ * input tokens) into h_ids; synchronises with the model stream. */
+VRT_API int vrt_batch_last_ids(vrt_batch* b, uint32_t count, uint32_t* h_ids);
+/* Last step's logits of `seq` (vocab floats; needs keep_logits). */
+VRT_API int vrt_batch_logits(vrt_batch* b, uint32_t seq, float* h_logits);
+
 /* ------------------------------------------------------ tokenizer (host)
  * The GGUF vocabulary's tokenizer with the reference's rules
  * (src/gemma3.cpp:289-454 index, 1895-2062 tokenize, 1237-1299 pieces); no

@@ -1,0 +1,140 @@
+"""Batched decode of independent sequences (vrt_batch_*) against decoding each
+sequence alone.
+
+Per sequence: the greedy stream equals the CPU oracle's for that prompt,
+except from a step whose oracle top-2 margin is below 1e-3 on; the last
+step's logits are within atol/rtol 1e-3 of the single-sequence path fed the
+same tokens.  Sequences sit at different positions (prompts of different
+lengths, crossing the tiny window of 8), and a step over the first `count`
+sequences leaves the others untouched.
+"""
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth_gguf as sg
+import vrt
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 1e-3, 1e-3
+
+
+def _close(a, b, atol=ATOL, rtol=RTOL):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    err = np.abs(a - b)
+    bound = atol + rtol * np.abs(b)
+    assert np.all(err <= bound), f"max err {err.max():.3g} (worst ratio {(err / bound).max():.3g})"
+
+
+def _agree(gpu, ref, margins):
+    for i, (a, b) in enumerate(zip(gpu, ref)):
+        if a != b:
+            assert margins[i] < 1e-3, f"step {i}: {a} vs {b}, margin {margins[i]}"
+            return False
+    return True
+
+
+def _single_logits(m, prompt, generated):
+    """Logits after feeding prompt + generated[:-1] one token at a time."""
+    m.reset()
+    toks = list(prompt) + list(generated[:-1])
+    for p, t in enumerate(toks):
+        m.decode(t, p, 1)
+    return m.logits()
+
+
+@pytest.mark.parametrize("name,seed", [("tiny", 1234), ("tiny-gqa", 4321)])
+def test_batch_vs_oracle_tiny(ctx, model_dir, name, seed):
+    path = sg.cached_model(sg.SHAPES[name], seed, model_dir)
+    model = vrt.Model(ctx, path, max_positions=64)
+    single = vrt.Model(ctx, path, max_positions=64, prefill_chunk=1)
+    o = O.Oracle(path)
+    rng = np.random.default_rng(seed)
+    prompts = [[2] + rng.integers(3, o.vocab, n - 1).tolist() for n in (3, 9, 14, 1 + 1, 21)]
+    b = vrt.Batch(model, 6, 48, keep_logits=True)
+    for i, p in enumerate(prompts):
+        b.prefill(i, p)
+    steps = 12
+    b.decode_steps(len(prompts), steps)
+    for i, p in enumerate(prompts):
+        ids, pos = b.read(i)
+        assert len(ids) == steps + 1 and pos == len(p) + steps
+        ref, margins = o.generate(p, steps + 1, margins=True)
+        if _agree(ids, ref, margins):
+            _close(b.logits(i), _single_logits(single, p, ids))
+    # a shorter step count leaves sequences >= count alone
+    before = [b.read(i) for i in range(len(prompts))]
+    b.decode_steps(2, 3)
+    after = [b.read(i) for i in range(len(prompts))]
+    for i in range(len(prompts)):
+        if i < 2:
+            assert after[i][1] == before[i][1] + 3 and after[i][0][:len(before[i][0])] == before[i][0]
+        else:
+            assert after[i] == before[i]
+    b.close()
+
+
+def test_batch_270m_vs_single(ctx):
+    """270M shape, 16 sequences with 24..54-token prompts, 6 steps."""
+    shape = sg.SHAPES["270m"]
+    cfg = vrt.Gemma3Config.from_shape(shape)
+    model = vrt.Model(ctx, None, config=cfg, seed=2024, max_positions=128)
+    single = vrt.Model(ctx, None, config=cfg, seed=2024, max_positions=128, prefill_chunk=1)
+    rng = np.random.default_rng(5)
+    prompts = [[2] + rng.integers(3, shape.vocab_size, 23 + 2 * i).tolist() for i in range(16)]
+    b = vrt.Batch(model, 16, 96, keep_logits=True)
+    for i, p in enumerate(prompts):
+        b.prefill(i, p)
+    b.decode_steps(16, 6)
+    for i in (0, 7, 15):
+        ids, pos = b.read(i)
+        ref = single.generate(prompts[i], 7)
+        lg = _single_logits(single, prompts[i], ids)
+        top2 = np.sort(lg)[-2:]
+        if ids == ref or top2[1] - top2[0] < 1e-3:
+            _close(b.logits(i), lg)
+        else:
+            raise AssertionError(f"sequence {i}: batch {ids} vs single {ref}")
+    b.close()
+
+
+def test_batch_27b_slice_vs_oracle(ctx):
+    """27B widths (G = 2, hd 128, ffn 21504) on 6 layers, 3 sequences."""
+    shape = sg.SHAPES["27b"].with_(block_count=6, vocab_size=16384, name="27b-slice")
+    cfg = vrt.Gemma3Config.from_shape(shape)
+    model = vrt.Model(ctx, None, config=cfg, seed=27, max_positions=32)
+    o = O.Oracle(shape=shape, seed=27, threads=16, max_positions=32)
+    rng = np.random.default_rng(27)
+    prompts = [[2] + rng.integers(3, shape.vocab_size, n).tolist() for n in (4, 9, 6)]
+    b = vrt.Batch(model, 3, 24)
+    for i, p in enumerate(prompts):
+        b.prefill(i, p)
+    b.decode_steps(3, 4)
+    for i, p in enumerate(prompts):
+        ids, _ = b.read(i)
+        ref, margins = o.generate(p, 5, margins=True)
+        _agree(ids, ref, margins)
+    b.close()
+
+
+def test_batch_errors(ctx, model_dir):
+    path = sg.cached_model(sg.SHAPES["tiny"], 1234, model_dir)
+    model = vrt.Model(ctx, path, max_positions=32)
+    with pytest.raises(vrt.VrtError):
+        vrt.Batch(model, 4, 64)                # more positions than the model
+    b = vrt.Batch(model, 2, 16)
+    with pytest.raises(vrt.VrtError, match="not been prefilled"):
+        b.decode_steps(2, 1)
+    b.prefill(0, [2, 5, 6])
+    b.prefill(1, [2, 7])
+    with pytest.raises(vrt.VrtError, match="capacity"):
+        b.decode_steps(2, 20)
+    with pytest.raises(vrt.VrtError, match="vocabulary"):
+        b.prefill(0, [2, 10 ** 6])
+    with pytest.raises(vrt.VrtError, match="keep_logits"):
+        b.logits(0)
+    b.decode_steps(2, 2)
+    assert b.read(0)[1] == 5 and b.read(1)[1] == 4
+    b.close()

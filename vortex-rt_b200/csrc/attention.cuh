@@ -45,6 +45,11 @@ struct AttnParams {
     uint32_t splits;
     float* zero0;           // buffer this launch clears
     uint32_t zero0_count;
+    // batched decode: grid.z = sequence; per-sequence strides in floats (0
+    // for one sequence); pos, part_*, tickets are per sequence
+    uint64_t seq_qkv, seq_cache, seq_out;
+    __half* out_hi;         // when set: output as fp16 hi/lo (the o-projection
+    __half* out_lo;         //   GEMM operand) instead of fp32 `out`
 };
 
 template <int M>  // M = hd / 32 values per lane
@@ -93,8 +98,10 @@ __device__ __forceinline__ void load_kv_batch(float (&kb)[P][M], float (&vb)[P][
     }
 }
 
-// M = head_dim / 32, RG >= H / KV (1, 2, 4 or 8).
-template <int M, int RG>
+// M = head_dim / 32, RG >= H / KV (1, 2, 4 or 8).  BATCH: grid.z walks
+// independent sequences (per-sequence strides); the single-sequence
+// instantiation keeps z = 0 at compile time and its register budget.
+template <int M, int RG, bool BATCH>
 __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const AttnParams p) {
     constexpr int HD = M * 32;
     constexpr int P = AttnBatch<M>::P;
@@ -106,21 +113,32 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
 
     pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t g = blockIdx.y, s = blockIdx.x;
+    const uint32_t g = blockIdx.y, s = blockIdx.x, z = BATCH ? blockIdx.z : 0u;
+    // this sequence's pointers (z = 0 and zero strides for a single sequence)
+    const uint64_t zz = z;
+    const float* const qkv = p.qkv + zz * p.seq_qkv;
+    float* const k_cache = p.k_cache + zz * p.seq_cache;
+    float* const v_cache = p.v_cache + zz * p.seq_cache;
+    float* const part_ml = p.part_ml + zz * p.H * p.splits * 2;
+    float* const part_acc = p.part_acc + zz * p.H * p.splits * p.hd;
+    uint32_t* const tickets = p.tickets + zz * p.KV;
+    float* const out = p.out ? p.out + zz * p.seq_out : nullptr;
+    __half* const out_hi = p.out_hi ? p.out_hi + zz * p.seq_out : nullptr;
+    __half* const out_lo = p.out_lo ? p.out_lo + zz * p.seq_out : nullptr;
     const uint32_t R = p.H / p.KV, hd = p.hd;
 
     // Nothing the step chain writes is read before griddepcontrol.wait --
     // not even the position: under programmatic launch the previous step's
     // finalize may still be in flight when this grid starts.
     pdl_wait();
-    const uint32_t pos = *p.pos;
+    const uint32_t pos = p.pos[z];
     const uint32_t n = p.window ? min(pos + 1, p.window) : pos + 1;
     const uint32_t first = pos + 1 - n;  // oldest position attended
     const uint32_t chunk = (n + p.splits - 1) / p.splits;
     const uint32_t t0 = first + s * chunk;
     const uint32_t t1 = min(first + n, t0 + chunk);
-    const float* kc = p.k_cache + static_cast<uint64_t>(g) * p.cap * hd;
-    const float* vc = p.v_cache + static_cast<uint64_t>(g) * p.cap * hd;
+    const float* kc = k_cache + static_cast<uint64_t>(g) * p.cap * hd;
+    const float* vc = v_cache + static_cast<uint64_t>(g) * p.cap * hd;
 
     // the first batch of older positions is in flight during the query prologue
     float kb[P][M], vb[P][M];
@@ -137,7 +155,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
 
     // 1. queries
     for (uint32_t r = warp; r < R; r += kAttnWarps) {
-        const float* src = p.qkv + static_cast<uint64_t>(g * R + r) * hd;
+        const float* src = qkv + static_cast<uint64_t>(g * R + r) * hd;
         float v[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) v[m] = src[lane + 32 * m];
@@ -148,15 +166,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     // 2. the newest key/value
     const bool has_new = t0 < t1 && t1 == pos + 1;
     if (has_new && warp == 0) {
-        const float* ks = p.qkv + static_cast<uint64_t>(p.H) * hd + static_cast<uint64_t>(g) * hd;
-        const float* vs = p.qkv + static_cast<uint64_t>(p.H + p.KV) * hd + static_cast<uint64_t>(g) * hd;
+        const float* ks = qkv + static_cast<uint64_t>(p.H) * hd + static_cast<uint64_t>(g) * hd;
+        const float* vs = qkv + static_cast<uint64_t>(p.H + p.KV) * hd + static_cast<uint64_t>(g) * hd;
         float v[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) v[m] = ks[lane + 32 * m];
         head_norm_rope<M>(v, p.k_norm, cs, sn, hd, p.eps, lane);
         const uint32_t slot = pos % p.cap;
-        float* kd = p.k_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
-        float* vd = p.v_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
+        float* kd = k_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
+        float* vd = v_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
 #pragma unroll
         for (int m = 0; m < M; ++m) {
             const float vv = vs[lane + 32 * m];
@@ -257,18 +275,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
             for (int m = 0; m < M; ++m) a[m] = fmaf(w_acc[w][r][lane + 32 * m], f, a[m]);
         }
         const uint32_t h = g * R + r;
-        float* pa = p.part_acc + (static_cast<uint64_t>(h) * p.splits + s) * hd;
+        float* pa = part_acc + (static_cast<uint64_t>(h) * p.splits + s) * hd;
 #pragma unroll
         for (int m = 0; m < M; ++m) pa[lane + 32 * m] = a[m];
         if (lane == 0) {
-            p.part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2] = M_;
-            p.part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2 + 1] = L_;
+            part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2] = M_;
+            part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2 + 1] = L_;
         }
     }
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-        const uint32_t ticket = atomicAdd(p.tickets + g, 1u);
+        const uint32_t ticket = atomicAdd(tickets + g, 1u);
         last_flag = (ticket == p.splits - 1) ? 1u : 0u;
     }
     __syncthreads();
@@ -280,8 +298,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     const uint32_t used = min(p.splits, (n + chunk - 1) / chunk);
     for (uint32_t r = warp; r < R; r += kAttnWarps) {
         const uint32_t h = g * R + r;
-        const float* ml = p.part_ml + static_cast<uint64_t>(h) * p.splits * 2;
-        const float* pa = p.part_acc + static_cast<uint64_t>(h) * p.splits * hd;
+        const float* ml = part_ml + static_cast<uint64_t>(h) * p.splits * 2;
+        const float* pa = part_acc + static_cast<uint64_t>(h) * p.splits * hd;
         // split weights reuse the warp-merge buffer (free once this CTA's partial is out)
         float* fw = &w_acc[0][0][0] + r * (kAttnWarps * HD);
         float M_ = -INFINITY;
@@ -316,10 +334,20 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
             }
         }
         const float inv = 1.0f / L_;
+        if (out_hi) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) p.out[static_cast<uint64_t>(h) * hd + lane + 32 * m] = a[m] * inv;
+            for (int m = 0; m < M; ++m) {
+                __half hh, ll;
+                split_f16(a[m] * inv, hh, ll);
+                out_hi[static_cast<uint64_t>(h) * hd + lane + 32 * m] = hh;
+                out_lo[static_cast<uint64_t>(h) * hd + lane + 32 * m] = ll;
+            }
+        } else {
+#pragma unroll
+            for (int m = 0; m < M; ++m) out[static_cast<uint64_t>(h) * hd + lane + 32 * m] = a[m] * inv;
+        }
     }
-    if (tid == 0) p.tickets[g] = 0u;
+    if (tid == 0) tickets[g] = 0u;
 }
 
 }  // namespace vrt

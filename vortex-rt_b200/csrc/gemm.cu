@@ -67,7 +67,12 @@ static cudaError_t gemm_launch_t(const TmaMap& hi, const TmaMap& lo, const GemmP
 }
 
 cudaError_t gemm_q8t(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
-    return epi == kGemmStore ? gemm_launch_t<kGemmStore>(hi, lo, p, s) : gemm_launch_t<kGemmGeluSplit>(hi, lo, p, s);
+    switch (epi) {
+    case kGemmStore: return gemm_launch_t<kGemmStore>(hi, lo, p, s);
+    case kGemmGeluSplit: return gemm_launch_t<kGemmGeluSplit>(hi, lo, p, s);
+    case kGemmArgmax: return gemm_launch_t<kGemmArgmax>(hi, lo, p, s);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 // Split fp32 rows into fp16 hi/lo operands (x = hi + lo to ~2^-22 relative).

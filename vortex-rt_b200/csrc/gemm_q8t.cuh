@@ -43,6 +43,7 @@ namespace vrt {
 enum GemmEpi : int {
     kGemmStore = 0,      // y[m][n] fp32
     kGemmGeluSplit = 1,  // W rows are 8 gate + 8 up per group: act = gelu(gate) * up -> fp16 hi/lo (+ optional fp32)
+    kGemmArgmax = 2,     // per-row argmax key (atomicMax into keys[m]; ties -> lower index, NaN skipped) + optional y
 };
 
 constexpr int kGemmBM = 128;
@@ -73,6 +74,8 @@ struct GemmParams {
     __half* act_lo;
     float* act_f32;       // GeluSplit: optional fp32 copy
     uint32_t ld_act;
+    unsigned long long* keys;  // Argmax: [M] keys, zero before the launch
+    uint32_t row_base;         // Argmax: global index of weight row 0 (vocab shard)
     uint32_t* status;
 };
 
@@ -140,11 +143,6 @@ constexpr uint32_t kGemmIdesc = (1u << 4) | (static_cast<uint32_t>(kGemmBN >> 3)
 // tile with 128-byte rows and the 128B swizzle (16-byte chunk index XOR row % 8).
 __host__ __device__ inline uint32_t sw128_offset(uint32_t row, uint32_t col) {
     return (row >> 3) * 1024u + (row & 7u) * 128u + ((((col >> 3) ^ (row & 7u)) & 7u) << 4) + (col & 7u) * 2u;
-}
-
-__device__ __forceinline__ void split_f16(float w, __half& hi, __half& lo) {
-    hi = __float2half_rn(w);
-    lo = __float2half_rn(__fsub_rn(w, __half2float(hi)));
 }
 
 // Dequantise one K half (64 columns) of a raw stage (8 Q8T tiles = 128 rows x
@@ -322,12 +320,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[a]);
         }
+        unsigned long long best = 0ull;
 #pragma unroll
         for (int cl = 0; cl < kGemmEpiCols; cl += 32) {
             float* v = sum + cl;
             const uint32_t c0 = cb + cl;
             if (row >= p.m) continue;
-            if (EPI == kGemmStore) {
+            if (EPI == kGemmArgmax) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (!isnan(v[j])) {
+                        const unsigned long long key = argmax_key(v[j], p.row_base + n0 + c0 + j);
+                        best = key > best ? key : best;
+                    }
+                }
+                if (p.y) {
+                    float4* dst = reinterpret_cast<float4*>(p.y + static_cast<uint64_t>(row) * p.ldy + n0 + c0);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) dst[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+                }
+            } else if (EPI == kGemmStore) {
                 float4* dst = reinterpret_cast<float4*>(p.y + static_cast<uint64_t>(row) * p.ldy + n0 + c0);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
@@ -366,6 +378,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
         }
+        if (EPI == kGemmArgmax && best != 0ull) atomicMax(p.keys + row, best);
     }
     __syncwarp();  // reconverge each warp (lane 0 of warps 0 and 1 ran alone) before the CTA barrier
     if (!ok) atomicOr(p.status, kStatusWaitTimeout);

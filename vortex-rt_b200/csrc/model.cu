@@ -317,6 +317,33 @@ struct vrt_model {
     } pf;
 };
 
+// Independent sequences decoded together on one model: per-sequence KV
+// caches, device-resident tokens / positions, one step = one token for each
+// of the first `count` sequences, projections as tensor-core GEMMs with M =
+// count rows, the LM head as a GEMM with a fused per-row argmax.
+struct vrt_batch {
+    vrt_model* m = nullptr;
+    uint32_t S = 0, P = 0, out_cap = 0;
+    bool keep_logits = false;
+    void* mem = nullptr;                       // caches + step buffers
+    std::vector<float*> kc, vc;                // per layer: sequence 0's K / V cache, [S][KV][cap][hd]
+    std::vector<uint32_t> cap;
+    uint32_t* tokens = nullptr;                // [S]
+    uint32_t* pos = nullptr;                   // [S]
+    uint32_t* out_ids = nullptr;               // [S][out_cap]
+    uint32_t* out_count = nullptr;             // [S]
+    uint32_t* prompt = nullptr;                // [P] prefill staging
+    unsigned long long* keys = nullptr;        // [S]
+    uint32_t* tickets = nullptr;               // [S][KV]
+    float *h0, *h1, *qkv, *o, *dn, *hidden, *logits, *part_ml, *part_acc;
+    __half *xh, *xl, *ah, *al;
+    vrt::TmaMap xd_hi, xd_lo, xq_hi, xq_lo, xf_hi, xf_lo;
+    uint32_t max_splits = 0;
+    std::vector<uint32_t> host_pos;            // positions as the host last set them
+    cudaGraphExec_t graph = nullptr;
+    uint32_t graph_count = 0;
+};
+
 namespace vrt {
 
 static int nccl_load(Nccl& n) {
@@ -1216,14 +1243,40 @@ static bool prefill_supported(const vrt_model* m) {
            (2 * m->ffl) % kGemmBN == 0 && m->ffl % kTileCols == 0 && (G == 1 || G == 2 || G == 4 || G == 8);
 }
 
-// The prompt (already in m->prompt, n tokens) through every layer in chunks
-// of pf.cap tokens, then the fused LM head + argmax on the last token and the
-// decode finalize: the step state ends exactly as after a token-by-token
-// prefill (position n, first generated id emitted).
-static int prefill_batched(vrt_model* m, uint32_t n) {
+// Where a prefill writes: the sequence's KV caches (per layer base and
+// capacity, [KV][cap][hd]), its prompt ids on the device, and the last
+// prompt token's LM-head outputs.
+struct SeqTarget {
+    const uint32_t* prompt = nullptr;
+    std::vector<float*> kc, vc;
+    std::vector<uint32_t> cap;
+    uint32_t positions = 0;              // capacity the caches were sized for
+    unsigned long long* key = nullptr;   // argmax key (zero on entry)
+    float* hidden = nullptr;             // normed hidden of the last token
+    float* logits = nullptr;             // optional full logits of the last token
+};
+
+static SeqTarget model_target(vrt_model* m) {
+    SeqTarget t;
+    t.prompt = m->prompt;
+    for (const auto& L : m->layers) {
+        t.kc.push_back(L.k_cache);
+        t.vc.push_back(L.v_cache);
+        t.cap.push_back(L.cap);
+    }
+    t.positions = m->P;
+    t.key = &m->st->key;
+    t.hidden = m->hidden;
+    t.logits = m->logits;
+    return t;
+}
+
+// The prompt (t.prompt, n tokens) through every layer in chunks of pf.cap
+// tokens, then the fused LM head + argmax on the last token.
+static int prefill_layers(vrt_model* m, const SeqTarget& t, uint32_t n) {
     const auto& c = m->cfg;
     const uint32_t want = m->opt.prefill_chunk ? m->opt.prefill_chunk : 2048u;
-    VRT_TRY(prefill_alloc(m, std::min(want, m->P)));
+    VRT_TRY(prefill_alloc(m, std::min(want, t.positions)));
     auto& B = m->pf;
     cudaStream_t s = m->ctx->stream;
     const uint32_t d = c.embedding_length, hd = c.head_dim, G = m->Hl / m->KVl;
@@ -1249,7 +1302,7 @@ static int prefill_batched(vrt_model* m, uint32_t n) {
     for (uint32_t p0 = 0; p0 < n; p0 += B.cap) {
         const uint32_t nc = std::min(B.cap, n - p0);
         last = nc;
-        embed_rows_kernel<<<nc, kRowThreads, 0, s>>>(m->arena + m->embd, m->prompt + p0, c.vocab_size, d,
+        embed_rows_kernel<<<nc, kRowThreads, 0, s>>>(m->arena + m->embd, t.prompt + p0, c.vocab_size, d,
                                                     std::sqrt(static_cast<float>(d)), F(m->layers[0].n_attn),
                                                     c.rms_epsilon, B.h0, B.xh, B.xl, status);
         VRT_CUDA(cudaGetLastError());
@@ -1267,9 +1320,9 @@ static int prefill_batched(vrt_model* m, uint32_t n) {
             a.q = B.q;
             a.k = B.k;
             a.v = B.v;
-            a.k_cache = L.k_cache;
-            a.v_cache = L.v_cache;
-            a.cap = L.cap;
+            a.k_cache = t.kc[l];
+            a.v_cache = t.vc[l];
+            a.cap = t.cap[l];
             a.window = L.global ? 0u : c.sliding_window;
             a.p0 = p0;
             a.n = nc;
@@ -1279,7 +1332,7 @@ static int prefill_batched(vrt_model* m, uint32_t n) {
             a.out_hi = B.xh;
             a.out_lo = B.xl;
             VRT_CUDA(prefill_attn_launch(a, hd, G, s));
-            kv_store_kernel<<<dim3(nc, m->KVl), 128, 0, s>>>(B.k, B.v, L.k_cache, L.v_cache, L.cap, m->KVl, hd, p0, nc);
+            kv_store_kernel<<<dim3(nc, m->KVl), 128, 0, s>>>(B.k, B.v, t.kc[l], t.vc[l], t.cap[l], m->KVl, hd, p0, nc);
             VRT_CUDA(cudaGetLastError());
             VRT_TRY(gemm(kGemmStore, B.xq_hi, B.xq_lo, m->arena + L.o, d, m->qwl, nc, B.o, nullptr, nullptr));
             resid_rows_kernel<<<nc, kRowThreads, 0, s>>>(B.o, B.h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
@@ -1300,16 +1353,129 @@ static int prefill_batched(vrt_model* m, uint32_t n) {
     p.h_prev = B.h1 + static_cast<uint64_t>(last - 1) * d;
     p.w_post = F(lastL.n_post_ffw);
     p.w_pre = F(m->out_norm);
-    p.h_out = m->hidden;
-    p.y = m->logits;
-    p.amax = &m->st->key;
+    p.h_out = t.hidden;
+    p.y = t.logits;
+    p.amax = t.key;
     p.row_base = m->vocab_lo;
     p.status = status;
     p.eps = c.rms_epsilon;
     VRT_CUDA(gemv_q8t(kProResidFinal, kEpiArgmax, p, gemv_grid(m->ctx->prop.multiProcessorCount, p.rows), s, false));
-    VRT_CUDA(launch(finalize_decode_kernel, dim3(1), dim3(1), 0, s, false, m->st, c.vocab_size, m->out_ids, kMaxSteps,
-                    TpParams{}));
     return VRT_OK;
+}
+
+// The model's own sequence: the step state ends exactly as after a
+// token-by-token prefill (position n, first generated id emitted).
+static int prefill_batched(vrt_model* m, uint32_t n) {
+    VRT_TRY(prefill_layers(m, model_target(m), n));
+    VRT_CUDA(launch(finalize_decode_kernel, dim3(1), dim3(1), 0, m->ctx->stream, false, m->st, m->cfg.vocab_size,
+                    m->out_ids, kMaxSteps, TpParams{}));
+    return VRT_OK;
+}
+
+// --------------------------------------------------------- batched decode
+
+static bool batch_supported(const vrt_model* m) {
+    return m->world <= 1 && prefill_supported(m) && m->cfg.vocab_size % kGemmBN == 0;
+}
+
+static uint32_t batch_splits(const vrt_batch* b, uint32_t count, uint32_t cap) {
+    const vrt_model* m = b->m;
+    const uint32_t ctas = count * m->KVl;
+    const uint32_t want = (2u * m->ctx->prop.multiProcessorCount + ctas - 1) / ctas;
+    return std::max(1u, std::min({want, (cap + 15) / 16, b->max_splits}));
+}
+
+// One decode step for sequences [0, count) on the model stream.
+static int batch_record_step(vrt_batch* b, uint32_t count) {
+    vrt_model* m = b->m;
+    const auto& c = m->cfg;
+    cudaStream_t s = m->ctx->stream;
+    const uint32_t d = c.embedding_length, hd = c.head_dim, qkvw = m->qwl + 2 * m->kwl;
+    uint32_t* status = &m->st->status;
+    auto F = [&](uint64_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+    auto gemm = [&](int epi, const TmaMap& hi, const TmaMap& lo, const uint8_t* w, uint32_t rows, uint32_t k,
+                    float* y, __half* ah, __half* al) -> int {
+        GemmParams p{};
+        p.w = w;
+        p.n = rows;
+        p.k = k;
+        p.m = count;
+        p.status = status;
+        p.y = y;
+        p.ldy = rows;
+        p.act_hi = ah;
+        p.act_lo = al;
+        p.ld_act = rows / 2;
+        p.keys = b->keys;
+        VRT_CUDA(gemm_q8t(epi, hi, lo, p, s));
+        return VRT_OK;
+    };
+    embed_rows_kernel<<<count, kRowThreads, 0, s>>>(m->arena + m->embd, b->tokens, c.vocab_size, d,
+                                                   std::sqrt(static_cast<float>(d)), F(m->layers[0].n_attn),
+                                                   c.rms_epsilon, b->h0, b->xh, b->xl, status);
+    VRT_CUDA(cudaGetLastError());
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const auto& L = m->layers[l];
+        if (l > 0) {
+            resid_rows_kernel<<<count, kRowThreads, 0, s>>>(b->dn, b->h1, F(m->layers[l - 1].n_post_ffw), F(L.n_attn),
+                                                           c.rms_epsilon, d, b->h0, b->xh, b->xl, status);
+            VRT_CUDA(cudaGetLastError());
+        }
+        VRT_TRY(gemm(kGemmStore, b->xd_hi, b->xd_lo, m->arena + L.qkv, qkvw, d, b->qkv, nullptr, nullptr));
+        AttnParams a{};
+        a.qkv = b->qkv;
+        a.q_norm = F(L.n_q);
+        a.k_norm = F(L.n_k);
+        a.rope_cos = L.global ? m->rope_cos_g : m->rope_cos_l;
+        a.rope_sin = L.global ? m->rope_sin_g : m->rope_sin_l;
+        a.k_cache = b->kc[l];
+        a.v_cache = b->vc[l];
+        a.cap = b->cap[l];
+        a.window = L.global ? 0u : c.sliding_window;
+        a.pos = b->pos;
+        a.H = m->Hl;
+        a.KV = m->KVl;
+        a.hd = hd;
+        a.eps = c.rms_epsilon;
+        a.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+        a.part_ml = b->part_ml;
+        a.part_acc = b->part_acc;
+        a.tickets = b->tickets;
+        a.splits = batch_splits(b, count, b->cap[l]);
+        a.seq_qkv = qkvw;
+        a.seq_cache = static_cast<uint64_t>(m->KVl) * b->cap[l] * hd;
+        a.seq_out = m->qwl;
+        a.out_hi = b->xh;
+        a.out_lo = b->xl;
+        VRT_CUDA(attention_launch(a, dim3(a.splits, m->KVl, count), s, false));
+        VRT_TRY(gemm(kGemmStore, b->xq_hi, b->xq_lo, m->arena + L.o, d, m->qwl, b->o, nullptr, nullptr));
+        resid_rows_kernel<<<count, kRowThreads, 0, s>>>(b->o, b->h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
+                                                       b->h1, b->xh, b->xl, status);
+        VRT_CUDA(cudaGetLastError());
+        VRT_TRY(gemm(kGemmGeluSplit, b->xd_hi, b->xd_lo, m->arena + L.gu, 2 * m->ffl, d, nullptr, b->ah, b->al));
+        VRT_TRY(gemm(kGemmStore, b->xf_hi, b->xf_lo, m->arena + L.down, d, m->ffl, b->dn, nullptr, nullptr));
+    }
+    const auto& lastL = m->layers[c.block_count - 1];
+    final_rows_kernel<<<count, kRowThreads, 0, s>>>(b->dn, b->h1, F(lastL.n_post_ffw), F(m->out_norm), c.rms_epsilon, d,
+                                                   b->hidden, b->xh, b->xl, status);
+    VRT_CUDA(cudaGetLastError());
+    VRT_TRY(gemm(kGemmArgmax, b->xd_hi, b->xd_lo, m->arena + m->embd, c.vocab_size, d,
+                 b->keep_logits ? b->logits : nullptr, nullptr, nullptr));
+    batch_finalize_kernel<<<(count + 127) / 128, 128, 0, s>>>(b->keys, b->tokens, b->pos, b->out_ids, b->out_count,
+                                                             b->out_cap, 0, count, c.vocab_size, 0, status);
+    VRT_CUDA(cudaGetLastError());
+    return VRT_OK;
+}
+
+static void batch_free(vrt_batch* b) {
+    if (!b) return;
+    if (b->m) {
+        cudaSetDevice(b->m->ctx->device);
+        cudaStreamSynchronize(b->m->ctx->stream);
+    }
+    if (b->graph) cudaGraphExecDestroy(b->graph);
+    cudaFree(b->mem);
+    delete b;
 }
 
 static int device_status(vrt_model* m, uint32_t& status) {
@@ -1829,6 +1995,215 @@ int vrt_tp_unique_id(void* h_out128) {
     VRT_TRY(nccl_load(n));
     const int r = n.GetUniqueId(h_out128);
     if (r) return fail(VRT_E_CUDA, "ncclGetUniqueId failed: %s", n.GetErrorString(r));
+    return VRT_OK;
+}
+
+int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, int keep_logits, vrt_batch** out) {
+    clear_error();
+    if (!m || !out) return fail(VRT_E_INVALID, "null argument");
+    *out = nullptr;
+    if (!batch_supported(m)) {
+        return fail(VRT_E_UNSUPPORTED, "batched decode needs one GPU (tp_world <= 1), 128-multiple projection widths, "
+                                       "1/2/4/8 query heads per KV head and a 128-multiple vocabulary");
+    }
+    if (max_seqs == 0 || max_seqs > 4096) return fail(VRT_E_INVALID, "max_seqs must be 1..4096");
+    if (max_positions == 0 || max_positions > m->P) {
+        return fail(VRT_E_INVALID, "batch max_positions must be 1..%u (the model's positions)", m->P);
+    }
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    std::unique_ptr<vrt_batch> b(new vrt_batch());
+    b->m = m;
+    b->S = max_seqs;
+    b->P = max_positions;
+    b->out_cap = max_positions;
+    b->keep_logits = keep_logits != 0;
+    const auto& c = m->cfg;
+    const uint64_t S = max_seqs, d = c.embedding_length, hd = c.head_dim;
+    b->max_splits = std::min<uint32_t>(32u, kAttnWarps * c.head_dim);
+    std::vector<uint64_t> sizes;  // bytes, 256-aligned pieces in this order
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const uint32_t cap = m->layers[l].global ? max_positions : std::min(c.sliding_window, max_positions);
+        b->cap.push_back(cap);
+        sizes.push_back(S * m->KVl * cap * hd * 4);  // K
+        sizes.push_back(S * m->KVl * cap * hd * 4);  // V
+    }
+    const uint64_t xw = std::max<uint64_t>(d, m->qwl);
+    const uint64_t fixed[] = {S * 4, S * 4, S * b->out_cap * 4, S * 4, uint64_t(max_positions) * 4, S * 8,
+                              S * m->KVl * 4,
+                              S * d * 4, S * d * 4, S * (m->qwl + 2ull * m->kwl) * 4, S * d * 4, S * d * 4, S * d * 4,
+                              b->keep_logits ? S * c.vocab_size * 4 : 0,
+                              S * m->Hl * b->max_splits * 2 * 4, S * m->Hl * b->max_splits * hd * 4,
+                              S * xw * 2, S * xw * 2, S * m->ffl * 2, S * m->ffl * 2};
+    for (auto x : fixed) sizes.push_back(x);
+    uint64_t total = 0;
+    for (auto x : sizes) total += align256(x);
+    VRT_CUDA(cudaMalloc(&b->mem, total));
+    VRT_CUDA(cudaMemsetAsync(b->mem, 0, total, m->ctx->stream));
+    uint8_t* p = static_cast<uint8_t*>(b->mem);
+    size_t i = 0;
+    auto take = [&]() {
+        uint8_t* q = p;
+        p += align256(sizes[i++]);
+        return q;
+    };
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        b->kc.push_back(reinterpret_cast<float*>(take()));
+        b->vc.push_back(reinterpret_cast<float*>(take()));
+    }
+    b->tokens = reinterpret_cast<uint32_t*>(take());
+    b->pos = reinterpret_cast<uint32_t*>(take());
+    b->out_ids = reinterpret_cast<uint32_t*>(take());
+    b->out_count = reinterpret_cast<uint32_t*>(take());
+    b->prompt = reinterpret_cast<uint32_t*>(take());
+    b->keys = reinterpret_cast<unsigned long long*>(take());
+    b->tickets = reinterpret_cast<uint32_t*>(take());
+    float** fl[] = {&b->h0, &b->h1, &b->qkv, &b->o, &b->dn, &b->hidden, &b->logits, &b->part_ml, &b->part_acc};
+    for (auto f : fl) *f = reinterpret_cast<float*>(take());
+    if (!b->keep_logits) b->logits = nullptr;
+    __half** hl[] = {&b->xh, &b->xl, &b->ah, &b->al};
+    for (auto h : hl) *h = reinterpret_cast<__half*>(take());
+    VRT_TRY(make_f16_tmap(&b->xd_hi, b->xh, S, d));
+    VRT_TRY(make_f16_tmap(&b->xd_lo, b->xl, S, d));
+    VRT_TRY(make_f16_tmap(&b->xq_hi, b->xh, S, m->qwl));
+    VRT_TRY(make_f16_tmap(&b->xq_lo, b->xl, S, m->qwl));
+    VRT_TRY(make_f16_tmap(&b->xf_hi, b->ah, S, m->ffl));
+    VRT_TRY(make_f16_tmap(&b->xf_lo, b->al, S, m->ffl));
+    b->host_pos.assign(max_seqs, 0);
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    *out = b.release();
+    return VRT_OK;
+}
+
+int vrt_batch_destroy(vrt_batch* b) {
+    batch_free(b);
+    return VRT_OK;
+}
+
+int vrt_batch_prefill(vrt_batch* b, uint32_t seq, const uint32_t* h_prompt, uint32_t n) {
+    clear_error();
+    if (!b || (!h_prompt && n)) return fail(VRT_E_INVALID, "null argument");
+    vrt_model* m = b->m;
+    const auto& c = m->cfg;
+    if (seq >= b->S) return fail(VRT_E_INVALID, "sequence %u outside the batch of %u", seq, b->S);
+    if (n == 0) return fail(VRT_E_INVALID, "Gemma 3 prompt produced no input tokens");
+    if (n > b->P) return fail(VRT_E_STATE, "prompt of %u tokens exceeds the batch capacity %u", n, b->P);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (h_prompt[i] >= c.vocab_size) return fail(VRT_E_INVALID, "Token id is outside Gemma 3 vocabulary");
+    }
+    cudaStream_t s = m->ctx->stream;
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    VRT_CUDA(cudaMemcpyAsync(b->prompt, h_prompt, 4ull * n, cudaMemcpyHostToDevice, s));
+    VRT_CUDA(cudaMemsetAsync(&m->st->status, 0, 4, s));
+    SeqTarget t;
+    t.prompt = b->prompt;
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+        const uint64_t off = static_cast<uint64_t>(seq) * m->KVl * b->cap[l] * c.head_dim;
+        t.kc.push_back(b->kc[l] + off);
+        t.vc.push_back(b->vc[l] + off);
+        t.cap.push_back(b->cap[l]);
+    }
+    t.positions = b->P;
+    t.key = b->keys + seq;
+    t.hidden = b->hidden + static_cast<uint64_t>(seq) * c.embedding_length;
+    t.logits = b->keep_logits ? b->logits + static_cast<uint64_t>(seq) * c.vocab_size : nullptr;
+    VRT_CUDA(cudaMemsetAsync(t.key, 0, 8, s));
+    VRT_TRY(prefill_layers(m, t, n));
+    batch_finalize_kernel<<<1, 1, 0, s>>>(b->keys, b->tokens, b->pos, b->out_ids, b->out_count, b->out_cap, seq, 1,
+                                          c.vocab_size, n, &m->st->status);
+    VRT_CUDA(cudaGetLastError());
+    uint32_t status = 0;
+    VRT_CUDA(cudaMemcpyAsync(&status, &m->st->status, 4, cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    if (status) return fail(status & kStatusWaitTimeout ? VRT_E_TIMEOUT : VRT_E_NUMERIC, "batch prefill: device status 0x%x", status);
+    b->host_pos[seq] = n;
+    return VRT_OK;
+}
+
+int vrt_batch_decode_steps(vrt_batch* b, uint32_t count, uint32_t steps) {
+    clear_error();
+    if (!b) return fail(VRT_E_INVALID, "null batch");
+    if (count == 0 || count > b->S) return fail(VRT_E_INVALID, "count must be 1..%u", b->S);
+    for (uint32_t i = 0; i < count; ++i) {
+        if (b->host_pos[i] == 0) return fail(VRT_E_STATE, "sequence %u has not been prefilled", i);
+        if (b->host_pos[i] + steps > b->P) return fail(VRT_E_STATE, "sequence %u would exceed the batch capacity", i);
+    }
+    vrt_model* m = b->m;
+    cudaStream_t s = m->ctx->stream;
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    if (m->opt.use_graph && (!b->graph || b->graph_count != count)) {
+        if (b->graph) {
+            VRT_CUDA(cudaStreamSynchronize(s));
+            cudaGraphExecDestroy(b->graph);
+            b->graph = nullptr;
+        }
+        cudaGraph_t g = nullptr;
+        VRT_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        const int rc = batch_record_step(b, count);
+        const cudaError_t e = cudaStreamEndCapture(s, &g);
+        if (rc != VRT_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture", __FILE__, __LINE__);
+        const cudaError_t ei = cudaGraphInstantiate(&b->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) return cuda_fail(ei, "cudaGraphInstantiate", __FILE__, __LINE__);
+        b->graph_count = count;
+    }
+    for (uint32_t i = 0; i < steps; ++i) {
+        if (b->graph) {
+            VRT_CUDA(cudaGraphLaunch(b->graph, s));
+        } else {
+            VRT_TRY(batch_record_step(b, count));
+        }
+    }
+    for (uint32_t i = 0; i < count; ++i) b->host_pos[i] += steps;
+    return VRT_OK;
+}
+
+int vrt_batch_read(vrt_batch* b, uint32_t seq, uint32_t* h_ids, uint32_t cap, uint32_t* h_count,
+                   uint32_t* h_position) {
+    clear_error();
+    if (!b || !h_count || (cap && !h_ids)) return fail(VRT_E_INVALID, "null argument");
+    if (seq >= b->S) return fail(VRT_E_INVALID, "sequence %u outside the batch of %u", seq, b->S);
+    vrt_model* m = b->m;
+    cudaStream_t s = m->ctx->stream;
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    uint32_t cnt = 0, pos = 0, status = 0;
+    VRT_CUDA(cudaMemcpyAsync(&cnt, b->out_count + seq, 4, cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaMemcpyAsync(&pos, b->pos + seq, 4, cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaMemcpyAsync(&status, &m->st->status, 4, cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaStreamSynchronize(s));
+    if (status) return fail(status & kStatusWaitTimeout ? VRT_E_TIMEOUT : VRT_E_NUMERIC, "batch decode: device status 0x%x", status);
+    const uint32_t k = std::min({cnt, cap, b->out_cap});
+    if (k) {
+        VRT_CUDA(cudaMemcpy(h_ids, b->out_ids + static_cast<uint64_t>(seq) * b->out_cap, 4ull * k, cudaMemcpyDeviceToHost));
+    }
+    *h_count = cnt;
+    if (h_position) *h_position = pos;
+    return VRT_OK;
+}
+
+int vrt_batch_last_ids(vrt_batch* b, uint32_t count, uint32_t* h_ids) {
+    clear_error();
+    if (!b || !h_ids) return fail(VRT_E_INVALID, "null argument");
+    if (count > b->S) return fail(VRT_E_INVALID, "count must be <= %u", b->S);
+    VRT_CUDA(cudaSetDevice(b->m->ctx->device));
+    VRT_CUDA(cudaMemcpyAsync(h_ids, b->tokens, 4ull * count, cudaMemcpyDeviceToHost, b->m->ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(b->m->ctx->stream));
+    return VRT_OK;
+}
+
+int vrt_batch_logits(vrt_batch* b, uint32_t seq, float* h_logits) {
+    clear_error();
+    if (!b || !h_logits) return fail(VRT_E_INVALID, "null argument");
+    if (!b->keep_logits) return fail(VRT_E_STATE, "batch created without keep_logits");
+    if (seq >= b->S) return fail(VRT_E_INVALID, "sequence %u outside the batch of %u", seq, b->S);
+    const uint32_t V = b->m->cfg.vocab_size;
+    VRT_CUDA(cudaSetDevice(b->m->ctx->device));
+    VRT_CUDA(cudaStreamSynchronize(b->m->ctx->stream));
+    VRT_CUDA(cudaMemcpy(h_logits, b->logits + static_cast<uint64_t>(seq) * V, 4ull * V, cudaMemcpyDeviceToHost));
     return VRT_OK;
 }
 

@@ -117,6 +117,71 @@ __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(const float* y,
     }
 }
 
+// Row m: h = rms_norm_inplace(y, w_post) + h_prev, then the output norm in
+// the rms_norm_inplace form x * (scale * w) (the LM-head prologue) ->
+// hidden (fp32) and x_hi / x_lo (the LM-head GEMM operand).
+__global__ void __launch_bounds__(kRowThreads) final_rows_kernel(const float* y, const float* h_prev,
+                                                                 const float* w_post, const float* w_out, float eps,
+                                                                 uint32_t d, float* hidden, __half* x_hi, __half* x_lo,
+                                                                 uint32_t* status) {
+    __shared__ double red[kRowThreads / 32];
+    const uint64_t base = static_cast<uint64_t>(blockIdx.x) * d;
+    float a[kRowMaxPerThread];
+    double so = 0.0;
+#pragma unroll
+    for (int u = 0; u < kRowMaxPerThread; ++u) {
+        const uint32_t k = threadIdx.x + u * kRowThreads;
+        a[u] = k < d ? y[base + k] : 0.0f;
+        so += static_cast<double>(a[u]) * static_cast<double>(a[u]);
+    }
+    so = block_sum_f64(so, red);
+    const float ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(d)) + eps);
+    double ss = 0.0;
+    bool bad = false;
+#pragma unroll
+    for (int u = 0; u < kRowMaxPerThread; ++u) {
+        const uint32_t k = threadIdx.x + u * kRowThreads;
+        if (k < d) {
+            const float h = __fadd_rn(__fmul_rn(a[u], __fmul_rn(ps, w_post[k])), h_prev[base + k]);
+            a[u] = h;
+            bad |= !isfinite(h);
+            ss += static_cast<double>(h) * static_cast<double>(h);
+        }
+    }
+    if (bad) atomicOr(status, kStatusNonFinite);
+    ss = block_sum_f64(ss, red);
+    const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(d)) + eps);
+#pragma unroll
+    for (int u = 0; u < kRowMaxPerThread; ++u) {
+        const uint32_t k = threadIdx.x + u * kRowThreads;
+        if (k < d) {
+            const float v = __fmul_rn(a[u], __fmul_rn(sc, w_out[k]));
+            hidden[base + k] = v;
+            store_split(x_hi, x_lo, base + k, v);
+        }
+    }
+}
+
+// Batched decode: per sequence s < count, the LM-head argmax key -> next
+// token, position + 1, generated id appended (ring of out_cap per sequence).
+// With `first` set (after a prefill of n tokens) the position becomes n.
+__global__ void batch_finalize_kernel(unsigned long long* keys, uint32_t* tokens, uint32_t* pos, uint32_t* out_ids,
+                                      uint32_t* out_count, uint32_t out_cap, uint32_t s0, uint32_t count,
+                                      uint32_t vocab, uint32_t first_pos, uint32_t* status) {
+    const uint32_t s = s0 + blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= s0 + count) return;
+    uint32_t idx;
+    float val;
+    argmax_unkey(keys[s], &idx, &val);
+    keys[s] = 0ull;
+    if (idx >= vocab || !isfinite(val)) atomicOr(status, kStatusNonFinite);
+    const uint32_t c = first_pos ? 0u : out_count[s];
+    if (c < out_cap) out_ids[static_cast<uint64_t>(s) * out_cap + c] = idx;
+    out_count[s] = c + 1;
+    tokens[s] = idx < vocab ? idx : 0u;
+    pos[s] = first_pos ? first_pos : pos[s] + 1;
+}
+
 // Token m of the chunk (position p0 + m): q heads and k heads -> per-head
 // RMSNorm + RoPE -> q [n][H][hd], k [n][KV][hd]; v copied to v [n][KV][hd].
 template <int M>

@@ -133,8 +133,11 @@ cudaError_t argmax_unkey_launch(const unsigned long long* key, uint32_t* out, cu
 cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, bool pdl) {
     const uint32_t M = p.hd / 32, R = p.H / p.KV;
     const int rg = R <= 1 ? 1 : R <= 2 ? 2 : R <= 4 ? 4 : 8;
-#define VRT_A(MM, RR) \
-    if (M == MM && rg == RR) return launch(attention_decode_kernel<MM, RR>, grid, dim3(kAttnThreads), 0, s, pdl, p);
+    const bool batch = grid.z > 1;
+#define VRT_A(MM, RR)                                                                                          \
+    if (M == MM && rg == RR)                                                                                   \
+        return batch ? launch(attention_decode_kernel<MM, RR, true>, grid, dim3(kAttnThreads), 0, s, pdl, p)  \
+                     : launch(attention_decode_kernel<MM, RR, false>, grid, dim3(kAttnThreads), 0, s, pdl, p);
     VRT_A(2, 1) VRT_A(2, 2) VRT_A(2, 4) VRT_A(2, 8)
     VRT_A(4, 1) VRT_A(4, 2) VRT_A(4, 4) VRT_A(4, 8)
     VRT_A(8, 1) VRT_A(8, 2) VRT_A(8, 4) VRT_A(8, 8)

@@ -198,6 +198,13 @@ __host__ __device__ inline void argmax_unkey(unsigned long long key, uint32_t* i
     *index = 0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu);
 }
 
+// w = hi + lo with both terms fp16 (to ~2^-22 relative): the tensor-core
+// operand form of an fp32 value.
+__device__ __forceinline__ void split_f16(float w, __half& hi, __half& lo) {
+    hi = __float2half_rn(w);
+    lo = __float2half_rn(__fsub_rn(w, __half2float(hi)));
+}
+
 template <typename T>
 __device__ __forceinline__ T warp_sum(T v) {
 #pragma unroll

@@ -11,6 +11,8 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+import sys
+import weakref
 
 import numpy as np
 
@@ -101,6 +103,13 @@ _SIGS = {
     "vrt_q8t_ffn": (_i, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp]),
     "vrt_q8t_lm_head_argmax": (_i, [_vp, _vp, _u32, _u32, _vp, _vp, _vp, _vp]),
     "vrt_q8t_gemm": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
+    "vrt_batch_create": (_i, [_vp, _u32, _u32, _i, _vp]),
+    "vrt_batch_destroy": (_i, [_vp]),
+    "vrt_batch_prefill": (_i, [_vp, _u32, _vp, _u32]),
+    "vrt_batch_decode_steps": (_i, [_vp, _u32, _u32]),
+    "vrt_batch_read": (_i, [_vp, _u32, _vp, _u32, _vp, _vp]),
+    "vrt_batch_logits": (_i, [_vp, _u32, _vp]),
+    "vrt_batch_last_ids": (_i, [_vp, _u32, _vp]),
     "vrt_q8t_gemm_gelu": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
     "vrt_model_options_default": (None, [C.POINTER(ModelOptions)]),
     "vrt_model_load": (_i, [_vp, C.c_char_p, C.POINTER(ModelOptions), C.POINTER(_vp)]),
@@ -162,6 +171,10 @@ class Context:
         self.h = _vp()
         check(lib().vrt_ctx_create(device, C.byref(self.h)))
         self._bufs: list[int] = []
+        self._children = weakref.WeakSet()  # models / batches: closed before the context
+
+    def _adopt(self, obj):
+        self._children.add(obj)
 
     def info(self) -> DeviceInfo:
         i = DeviceInfo()
@@ -195,7 +208,13 @@ class Context:
         return out
 
     def close(self):
-        if self.h:
+        if self.h and not sys.is_finalizing():  # at interpreter exit the CUDA runtime may already be gone
+            kids = list(self._children)
+            for k in kids:  # batches before the models they decode with
+                if isinstance(k, Batch):
+                    k.close()
+            for k in kids:
+                k.close()
             lib().vrt_ctx_destroy(self.h)
             self.h = _vp()
 
@@ -214,6 +233,9 @@ class Model:
                  tp_rank: int = 0, tp_world: int = 1, nccl_id: bytes | None = None,
                  tp_exchange: str = "peer", tp_wait_ms: int = 0, prefill_chunk: int = 0):
         self.ctx = ctx
+        self.h = _vp()
+        self._batches = weakref.WeakSet()
+        ctx._adopt(self)
         o = ModelOptions()
         lib().vrt_model_options_default(C.byref(o))
         o.max_positions = max_positions
@@ -234,7 +256,9 @@ class Model:
         check(lib().vrt_model_config(self.h, C.byref(self.config)))
 
     def close(self):
-        if self.h:
+        if self.h and not sys.is_finalizing():  # at interpreter exit the CUDA runtime may already be gone
+            for b in list(self._batches):
+                b.close()
             lib().vrt_model_destroy(self.h)
             self.h = _vp()
 
@@ -302,6 +326,47 @@ class Model:
         return out.reshape(c.block_count, c.embedding_length)
 
 
+class Batch:
+    """Independent sequences decoded together on one model (vrt_batch_*)."""
+
+    def __init__(self, model: "Model", max_seqs: int, max_positions: int, keep_logits: bool = False):
+        self.model = model
+        self.h = _vp()
+        model.ctx._adopt(self)
+        model._batches.add(self)
+        check(lib().vrt_batch_create(model.h, max_seqs, max_positions, int(keep_logits), C.byref(self.h)))
+
+    def close(self):
+        if self.h and not sys.is_finalizing():  # at interpreter exit the CUDA runtime may already be gone
+            lib().vrt_batch_destroy(self.h)
+            self.h = _vp()
+
+    __del__ = close
+
+    def prefill(self, seq: int, prompt):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        check(lib().vrt_batch_prefill(self.h, seq, _ptr(p), p.size))
+
+    def decode_steps(self, count: int, steps: int):
+        check(lib().vrt_batch_decode_steps(self.h, count, steps))
+
+    def read(self, seq: int, cap: int = 1 << 16) -> tuple[list[int], int]:
+        out = np.zeros(max(cap, 1), np.uint32)
+        n, pos = _u32(), _u32()
+        check(lib().vrt_batch_read(self.h, seq, _ptr(out), cap, C.byref(n), C.byref(pos)))
+        return out[:min(n.value, cap)].tolist(), pos.value
+
+    def logits(self, seq: int) -> np.ndarray:
+        out = np.zeros(self.model.config.vocab_size, np.float32)
+        check(lib().vrt_batch_logits(self.h, seq, _ptr(out)))
+        return out
+
+    def last_ids(self, count: int, out: np.ndarray | None = None) -> np.ndarray:
+        out = np.zeros(count, np.uint32) if out is None else out
+        check(lib().vrt_batch_last_ids(self.h, count, _ptr(out)))
+        return out
+
+
 class Tokenizer:
     """Host tokenizer of a GGUF vocabulary (vrt_tokenizer_*; no GPU)."""
 
@@ -310,7 +375,7 @@ class Tokenizer:
         check(lib().vrt_tokenizer_open(path.encode(), C.byref(self.h)))
 
     def close(self):
-        if self.h:
+        if self.h and not sys.is_finalizing():  # at interpreter exit the CUDA runtime may already be gone
             lib().vrt_tokenizer_close(self.h)
             self.h = _vp()
 
