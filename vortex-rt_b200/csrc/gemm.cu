@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -33,16 +34,16 @@ static EncodeTiledFn encode_fn() {
 }
 
 // Tensor map over a row-major fp16 matrix [rows][cols] (cols % 64 == 0, base
-// 16-byte aligned), box = 64 columns x 128 rows, 128B swizzle; rows past the
-// end read as zeros.
-int make_f16_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols) {
+// 16-byte aligned), box = 64 columns x box_rows rows (128 for the large-M
+// GEMM, 16 for the small-M form), 128B swizzle; rows past the end read as zeros.
+int make_f16_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
     static_assert(sizeof(TmaMap) == sizeof(CUtensorMap), "tensor map size");
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(VRT_E_UNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
     if (cols % kGemmBK || reinterpret_cast<uintptr_t>(base) % 16) return fail(VRT_E_INVALID, "fp16 operand layout");
     const cuuint64_t dims[2] = {cols, rows};
     const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), static_cast<cuuint32_t>(kGemmBM)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -64,6 +65,51 @@ static cudaError_t gemm_launch_t(const TmaMap& hi, const TmaMap& lo, const GemmP
     }
     const dim3 grid(p.n / kGemmBN, (p.m + kGemmBM - 1) / kGemmBM);
     return launch(q8t_gemm_kernel<EPI>, grid, dim3(kGemmThreads), kGemmSmemBytes, s, false, hi, lo, p);
+}
+
+template <int EPI, int NTMAX>
+static cudaError_t gemm_small_launch_t(const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
+    static uint64_t done = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    constexpr uint32_t smem = SmallGemmLayout<NTMAX>::kSmem;
+    if (dev < 64 && !(done & (1ull << dev))) {
+        e = cudaFuncSetAttribute(q8t_gemm_small_kernel<EPI, NTMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        done |= 1ull << dev;
+    }
+    const dim3 grid(p.n / kGemmBN, (p.m + p.nt - 1) / p.nt, p.ksplit);
+    return launch(q8t_gemm_small_kernel<EPI, NTMAX>, grid, dim3(kGemmThreads), smem, s, false, hi, lo, p);
+}
+
+template <int NTMAX>
+static cudaError_t gemm_small_epi(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
+    switch (epi) {
+    case kGemmStore: return gemm_small_launch_t<kGemmStore, NTMAX>(hi, lo, p, s);
+    case kGemmGeluSplit: return gemm_small_launch_t<kGemmGeluSplit, NTMAX>(hi, lo, p, s);
+    case kGemmArgmax: return gemm_small_launch_t<kGemmArgmax, NTMAX>(hi, lo, p, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t gemm_q8t_small(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
+    if (p.nt != 16 && p.nt != 32 && p.nt != 64 && p.nt != 128) return cudaErrorInvalidValue;
+    if (p.ksplit == 0 || (p.ksplit > 1 && (!p.ws || !p.tickets))) return cudaErrorInvalidValue;
+    return p.nt <= 64 ? gemm_small_epi<64>(epi, hi, lo, p, s) : gemm_small_epi<128>(epi, hi, lo, p, s);
+}
+
+// K splits for a small-M GEMM: enough CTAs for two per SM, at least two
+// 128-column K tiles per split, at most 16 splits.
+uint32_t gemm_small_ksplit(uint32_t n, uint32_t m, uint32_t k, int sms) {
+    const uint32_t tiles = (n / kGemmBN) * ((m + gemm_small_tile(m) - 1) / gemm_small_tile(m));
+    const uint32_t want = (2u * static_cast<uint32_t>(sms) + tiles - 1) / tiles;
+    const uint32_t kmax = std::max(1u, (k / kTileCols) / 2);
+    return std::max(1u, std::min({want, kmax, 16u}));
+}
+
+uint32_t gemm_small_tile(uint32_t m) {
+    return m <= 16 ? 16u : m <= 32 ? 32u : m <= 64 ? 64u : 128u;
 }
 
 cudaError_t gemm_q8t(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
@@ -123,19 +169,30 @@ static int gemm_common(vrt_ctx* ctx, int epi, const void* d_packed, uint32_t row
     VRT_CUDA(cudaSetDevice(ctx->device));
     const uint64_t xn = static_cast<uint64_t>(m) * cols;
     const uint64_t an = epi == kGemmGeluSplit ? static_cast<uint64_t>(m) * (rows / 2) : 0;
+    const bool small = m <= 128;  // weight rows on the MMA's 128 lanes, activation rows on N
+    const uint32_t nt = small ? gemm_small_tile(m) : 0u;
+    const uint32_t ks = small ? gemm_small_ksplit(rows, m, cols, ctx->prop.multiProcessorCount) : 1u;
+    const uint64_t ws_f = ks > 1 ? static_cast<uint64_t>(ks) * nt * rows : 0;   // partials (one token tile)
+    const uint64_t tk = small ? rows / kGemmBN : 0;
+    const uint64_t f16_bytes = ((2 * xn + 2 * an) * sizeof(__half) + 255) / 256 * 256;
     void* ws = nullptr;
-    VRT_TRY(ctx_workspace(ctx, (2 * xn + 2 * an) * sizeof(__half) + 256, &ws));
+    VRT_TRY(ctx_workspace(ctx, f16_bytes + ws_f * 4 + tk * 4 + 256, &ws));
     __half* xh = static_cast<__half*>(ws);
     __half* xl = xh + xn;
     VRT_CUDA(split_f16(d_x, xn, xh, xl, s));
     TmaMap th, tl;
-    VRT_TRY(make_f16_tmap(&th, xh, m, cols));
-    VRT_TRY(make_f16_tmap(&tl, xl, m, cols));
+    VRT_TRY(make_f16_tmap(&th, xh, m, cols, small ? 16u : 128u));
+    VRT_TRY(make_f16_tmap(&tl, xl, m, cols, small ? 16u : 128u));
     GemmParams p{};
     p.w = static_cast<const uint8_t*>(d_packed);
     p.n = rows;
     p.k = cols;
     p.m = m;
+    p.nt = nt;
+    p.ksplit = ks;
+    p.ws = ks > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + f16_bytes) : nullptr;
+    p.tickets = small ? reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + f16_bytes + ws_f * 4) : nullptr;
+    if (small) VRT_CUDA(cudaMemsetAsync(p.tickets, 0, tk * 4, s));
     uint32_t* status = reinterpret_cast<uint32_t*>(ctx->d_key + 1);  // word after the argmax key
     p.status = status;
     if (epi == kGemmStore) {
@@ -148,7 +205,7 @@ static int gemm_common(vrt_ctx* ctx, int epi, const void* d_packed, uint32_t row
         p.ld_act = rows / 2;
     }
     VRT_CUDA(cudaMemsetAsync(status, 0, 4, s));
-    VRT_CUDA(gemm_q8t(epi, th, tl, p, s));
+    VRT_CUDA(small ? gemm_q8t_small(epi, th, tl, p, s) : gemm_q8t(epi, th, tl, p, s));
     uint32_t st = 0;
     VRT_CUDA(cudaMemcpyAsync(&st, status, 4, cudaMemcpyDeviceToHost, s));
     VRT_CUDA(cudaStreamSynchronize(s));

@@ -76,6 +76,10 @@ struct GemmParams {
     uint32_t ld_act;
     unsigned long long* keys;  // Argmax: [M] keys, zero before the launch
     uint32_t row_base;         // Argmax: global index of weight row 0 (vocab shard)
+    uint32_t nt;               // small-M form: activation rows per CTA (16, 32, 64 or 128)
+    uint32_t ksplit;           // small-M form: CTAs along K per tile (partials in ws, last CTA reduces)
+    float* ws;                 // [ksplit][t_tiles * nt][n] partial sums (ksplit > 1)
+    uint32_t* tickets;         // [n / 128 * t_tiles], zero; reset by the reducing CTA
     uint32_t* status;
 };
 
@@ -115,6 +119,14 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                  : "memory");
+}
+
+// 8 consecutive fp32 accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // 32 consecutive fp32 accumulator columns of this warp's 32 TMEM lanes.
@@ -387,6 +399,250 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, 2 * kGemmBN);
+    }
+}
+
+// --------------------------------------------------------------- small M
+//
+// Batched decode form: the 128 lanes of the MMA carry weight rows and N
+// carries p.nt activation rows (16..128), so 32 sequences issue a quarter of
+// the tensor work of a 128-row tile.  The weight stream is the bottleneck at
+// small M, so this form keeps more of it in flight (operand stages sized for
+// NTMAX activation rows, 5-7 raw Q8T stages) and splits K across grid.z when
+// the tiles alone do not fill the SMs: each CTA sums a K range, non-final
+// CTAs leave fp32 partials in p.ws, and the last CTA of the tile (atomic
+// ticket) adds the splits in split order -- deterministic whichever CTA is
+// last -- and runs the epilogue.  Same dequantisation, hi/lo split and
+// chunked promotion as the large-M kernel.  Epilogue per token column,
+// writes coalesced across lanes: store, gelu(gate) * up (gate row r and up
+// row r + 8 of a 16-row group meet through a lane shuffle), or argmax (warp
+// max of the 64-bit keys, one atomicMax per token and warp).
+template <int NTMAX>
+struct SmallGemmLayout {
+    static constexpr int kXBytes = NTMAX * 128;                          // one activation operand tile
+    static constexpr int kStage = 2 * kXBytes + 2 * kGemmOpTile;         // x_hi, x_lo, w_hi, w_lo
+    static constexpr int kStages = 2;
+    static constexpr int kRaw =
+        (232448 - 1024 - kStages * kStage - 256) / kGemmRawBytes > 7 ? 7 : (232448 - 1024 - kStages * kStage - 256) / kGemmRawBytes;
+    static constexpr uint32_t kSmem = 1024 + kStages * kStage + kRaw * kGemmRawBytes + 8 * (2 * kStages + 2 * kRaw + 4) + 16;
+};
+
+template <int EPI, int NTMAX>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    q8t_gemm_small_kernel(const __grid_constant__ TmaMap x_hi, const __grid_constant__ TmaMap x_lo, const GemmParams p) {
+    using LY = SmallGemmLayout<NTMAX>;
+    constexpr int S = LY::kStages, R = LY::kRaw;
+    extern __shared__ uint8_t gsm_raw[];
+    __shared__ uint32_t last_cta;
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* ring = sm;
+    uint8_t* raw = sm + S * LY::kStage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(raw + R * kGemmRawBytes);
+    uint64_t* empty = full + S;
+    uint64_t* raw_full = empty + S;
+    uint64_t* raw_empty = raw_full + R;
+    uint64_t* acc_full = raw_empty + R;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t NT = p.nt;  // 16, 32, 64 or 128 (<= NTMAX)
+    const uint32_t n0 = blockIdx.x * kGemmBN, t0 = blockIdx.y * NT;
+    const uint32_t KTALL = p.k / kTileCols;
+    const uint32_t kt0 = KTALL * blockIdx.z / p.ksplit, kt1 = KTALL * (blockIdx.z + 1) / p.ksplit;
+    const uint32_t KT = kt1 - kt0, NI = 2 * KT;
+    const uint32_t NC = (NI + kGemmChunkStages - 1) / kGemmChunkStages;
+    const uint32_t tcols = NT < 16 ? 32u : 2u * NT;
+    const uint32_t idesc = (1u << 4) | ((NT >> 3) << 17) | (static_cast<uint32_t>(kGemmBN >> 4) << 24);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1 + 4);  // activation expect_tx + 4 dequant warps
+            mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < R; ++r) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], 4);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 8);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, tcols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        // weight stream only, up to R stages ahead of the dequantisation
+        if (lane == 0) {
+            const uint8_t* wg = p.w + static_cast<uint64_t>(n0 / kTileRows) * KTALL * kTileBytes;
+            for (uint32_t kt = 0; kt < KT; ++kt) {
+                const uint32_t r = kt % R;
+                if (kt >= static_cast<uint32_t>(R)) ok &= mbar_wait_bounded(&raw_empty[r], ((kt / R) - 1) & 1);
+                mbar_arrive_expect_tx(&raw_full[r], kGemmRawBytes);
+                for (int g = 0; g < kGemmBN / kTileRows; ++g) {
+                    bulk_copy_g2s(raw + r * kGemmRawBytes + g * kTileBytes,
+                                  wg + (static_cast<uint64_t>(g) * KTALL + kt0 + kt) * kTileBytes, kTileBytes,
+                                  &raw_full[r]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (uint32_t i = 0; i < NI; ++i) {
+                const uint32_t c = i / kGemmChunkStages, a = c & 1, first = i % kGemmChunkStages == 0;
+                if (first && c >= 2) ok &= mbar_wait_bounded(&acc_empty[a], ((c / 2) - 1) & 1);
+                const uint32_t s = i % S;
+                ok &= mbar_wait_bounded(&full[s], (i / S) & 1);
+                tc_fence_after();
+                const uint32_t base = smem_addr(ring + s * LY::kStage);
+                const uint32_t acc = tmem + a * NT;
+#pragma unroll
+                for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+                    const uint32_t o = kk * 32;
+                    const uint64_t xhi = sw128_desc(base + o), xlo = sw128_desc(base + LY::kXBytes + o);
+                    const uint64_t whi = sw128_desc(base + 2 * LY::kXBytes + o);
+                    const uint64_t wlo = sw128_desc(base + 2 * LY::kXBytes + kGemmOpTile + o);
+                    umma_f16(acc, whi, xhi, idesc, (first && kk == 0) ? 0u : 1u);
+                    umma_f16(acc, whi, xlo, idesc, 1u);
+                    umma_f16(acc, wlo, xhi, idesc, 1u);
+                }
+                umma_commit(&empty[s]);
+                if ((i + 1) % kGemmChunkStages == 0 || i + 1 == NI) umma_commit(&acc_full[a]);
+            }
+        }
+    } else if (warp < 6) {
+        const int t = tid - 64;
+        for (uint32_t kt = 0; kt < KT; ++kt) {
+            const uint32_t r = kt % R;
+            ok &= mbar_wait_bounded(&raw_full[r], (kt / R) & 1);
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t i = 2 * kt + h, s = i % S;
+                if (i >= static_cast<uint32_t>(S)) ok &= mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1);
+                uint8_t* st = ring + s * LY::kStage;
+                if (t == 0) {  // this stage's activation tiles (16-row TMA boxes)
+                    mbar_arrive_expect_tx(&full[s], 2 * NT * 128);
+                    const int kx = static_cast<int>((kt0 + kt) * kTileCols + h * kGemmBK);
+                    for (uint32_t r0 = 0; r0 < NT; r0 += 16) {
+                        tma_load_2d(st + r0 * 128, &x_hi, kx, static_cast<int>(t0 + r0), &full[s]);
+                        tma_load_2d(st + LY::kXBytes + r0 * 128, &x_lo, kx, static_cast<int>(t0 + r0), &full[s]);
+                    }
+                }
+                dequant_half(raw + r * kGemmRawBytes, t, h, st + 2 * LY::kXBytes, st + 2 * LY::kXBytes + kGemmOpTile);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[r]);
+        }
+    } else {
+        // epilogue: lanes = weight rows n0 + 32q + lane; this warp's token columns [cb, cb + NT/2)
+        const uint32_t q = warp & 3;
+        const uint32_t half_cols = NT / 2;
+        const uint32_t cb = ((warp - 6) >> 2) * half_cols;
+        const uint32_t row = n0 + 32 * q + lane;
+        float sum[NTMAX / 2];
+#pragma unroll
+        for (int j = 0; j < NTMAX / 2; ++j) sum[j] = 0.0f;
+        for (uint32_t c = 0; c < NC; ++c) {
+            const uint32_t a = c & 1;
+            ok &= mbar_wait_bounded(&acc_full[a], (c / 2) & 1);
+            tc_fence_after();
+#pragma unroll
+            for (int j0 = 0; j0 < NTMAX / 2; j0 += 8) {
+                if (static_cast<uint32_t>(j0) < half_cols) {
+                    uint32_t v[8];
+                    tmem_ld8(tmem + ((32 * q) << 16) + a * NT + cb + j0, v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) sum[j0 + e] = __fadd_rn(sum[j0 + e], __uint_as_float(v[e]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+        bool last = true;
+        if (p.ksplit > 1) {
+            // partials of this K range out; the last CTA of the tile adds all ranges in split order
+            const uint64_t mp = static_cast<uint64_t>(gridDim.y) * NT;  // padded token rows
+            float* mine = p.ws + static_cast<uint64_t>(blockIdx.z) * mp * p.n;
+#pragma unroll
+            for (int j = 0; j < NTMAX / 2; ++j) {
+                if (static_cast<uint32_t>(j) < half_cols) mine[(t0 + cb + j) * static_cast<uint64_t>(p.n) + row] = sum[j];
+            }
+            __threadfence();
+            named_bar_sync(2, 256);
+            if (warp == 6 && lane == 0) {
+                const uint32_t tk = atomicAdd(p.tickets + blockIdx.y * gridDim.x + blockIdx.x, 1u);
+                last_cta = tk == p.ksplit - 1 ? 1u : 0u;
+            }
+            named_bar_sync(2, 256);
+            last = last_cta != 0;
+            if (last) {
+                __threadfence();
+#pragma unroll
+                for (int j = 0; j < NTMAX / 2; ++j) {
+                    if (static_cast<uint32_t>(j) < half_cols) {
+                        float v = 0.0f;
+                        for (uint32_t z = 0; z < p.ksplit; ++z) {
+                            const float pz = z == blockIdx.z ? sum[j]
+                                                             : __ldcg(p.ws + static_cast<uint64_t>(z) * mp * p.n +
+                                                                      (t0 + cb + j) * static_cast<uint64_t>(p.n) + row);
+                            v = z == 0 ? pz : __fadd_rn(v, pz);
+                        }
+                        sum[j] = v;
+                    }
+                }
+                if (warp == 6 && lane == 0) p.tickets[blockIdx.y * gridDim.x + blockIdx.x] = 0u;
+            }
+        }
+        if (last) {
+#pragma unroll
+            for (int j = 0; j < NTMAX / 2; ++j) {
+                if (static_cast<uint32_t>(j) >= half_cols) continue;  // warp-uniform
+                const uint32_t tok = t0 + cb + j;
+                const float v = sum[j];
+                if (EPI == kGemmStore) {
+                    if (tok < p.m) p.y[static_cast<uint64_t>(tok) * p.ldy + row] = v;
+                } else if (EPI == kGemmGeluSplit) {
+                    const float up = __shfl_down_sync(0xffffffffu, v, 8);
+                    if (tok < p.m && (lane & 8) == 0) {
+                        const float act = __fmul_rn(gelu_tanh(v), up);
+                        const uint64_t o = static_cast<uint64_t>(tok) * p.ld_act + (row >> 4) * 8 + (lane & 7);
+                        __half hh, ll;
+                        split_f16(act, hh, ll);
+                        p.act_hi[o] = hh;
+                        p.act_lo[o] = ll;
+                        if (p.act_f32) p.act_f32[o] = act;
+                    }
+                } else {
+                    unsigned long long key = isnan(v) ? 0ull : argmax_key(v, p.row_base + row);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = other > key ? other : key;
+                    }
+                    if (tok < p.m) {
+                        if (p.y) p.y[static_cast<uint64_t>(tok) * p.ldy + row] = v;
+                        if (lane == 0 && key != 0ull) atomicMax(p.keys + tok, key);
+                    }
+                }
+            }
+        }
+    }
+    __syncwarp();
+    if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tcols);
     }
 }
 

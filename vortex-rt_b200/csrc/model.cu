@@ -337,8 +337,12 @@ struct vrt_batch {
     uint32_t* tickets = nullptr;               // [S][KV]
     float *h0, *h1, *qkv, *o, *dn, *hidden, *logits, *part_ml, *part_acc;
     __half *xh, *xl, *ah, *al;
-    vrt::TmaMap xd_hi, xd_lo, xq_hi, xq_lo, xf_hi, xf_lo;
+    vrt::TmaMap xd_hi, xd_lo, xq_hi, xq_lo, xf_hi, xf_lo;        // 16-row boxes: small-M GEMM (<= 128 sequences)
+    vrt::TmaMap Xd_hi, Xd_lo, Xq_hi, Xq_lo, Xf_hi, Xf_lo;        // 128-row boxes: large-M GEMM
     uint32_t max_splits = 0;
+    float* gws = nullptr;                      // small-M GEMM split-K partials
+    uint32_t* gtickets = nullptr;              // small-M GEMM reduction tickets (zero between launches)
+    uint64_t gws_floats = 0, gtickets_n = 0;
     std::vector<uint32_t> host_pos;            // positions as the host last set them
     cudaGraphExec_t graph = nullptr;
     uint32_t graph_count = 0;
@@ -1172,12 +1176,12 @@ static int prefill_alloc(vrt_model* m, uint32_t cap) {
         p += align256(f16[i] * 2);
     }
     VRT_CUDA(cudaMemsetAsync(B.mem, 0, total, m->ctx->stream));
-    VRT_TRY(make_f16_tmap(&B.xd_hi, B.xh, C, d));
-    VRT_TRY(make_f16_tmap(&B.xd_lo, B.xl, C, d));
-    VRT_TRY(make_f16_tmap(&B.xq_hi, B.xh, C, m->qwl));
-    VRT_TRY(make_f16_tmap(&B.xq_lo, B.xl, C, m->qwl));
-    VRT_TRY(make_f16_tmap(&B.xf_hi, B.ah, C, m->ffl));
-    VRT_TRY(make_f16_tmap(&B.xf_lo, B.al, C, m->ffl));
+    VRT_TRY(make_f16_tmap(&B.xd_hi, B.xh, C, d, 128));
+    VRT_TRY(make_f16_tmap(&B.xd_lo, B.xl, C, d, 128));
+    VRT_TRY(make_f16_tmap(&B.xq_hi, B.xh, C, m->qwl, 128));
+    VRT_TRY(make_f16_tmap(&B.xq_lo, B.xl, C, m->qwl, 128));
+    VRT_TRY(make_f16_tmap(&B.xf_hi, B.ah, C, m->ffl, 128));
+    VRT_TRY(make_f16_tmap(&B.xf_lo, B.al, C, m->ffl, 128));
     B.cap = cap;
     return VRT_OK;
 }
@@ -1385,6 +1389,41 @@ static uint32_t batch_splits(const vrt_batch* b, uint32_t count, uint32_t cap) {
     return std::max(1u, std::min({want, (cap + 15) / 16, b->max_splits}));
 }
 
+// Split-K workspace and tickets for the step's small-M GEMMs at `count` rows.
+static int batch_gemm_workspace(vrt_batch* b, uint32_t count) {
+    vrt_model* m = b->m;
+    const auto& c = m->cfg;
+    const int sms = m->ctx->prop.multiProcessorCount;
+    const uint32_t d = c.embedding_length;
+    const uint32_t shapes[][2] = {{m->qwl + 2 * m->kwl, d}, {d, m->qwl}, {2 * m->ffl, d}, {d, m->ffl}, {c.vocab_size, d}};
+    if (count > kGemmBM) return VRT_OK;  // large-M kernel: no split-K workspace
+    const uint32_t nt = gemm_small_tile(count), tt = (count + nt - 1) / nt;
+    uint64_t wsf = 0, tk = 0;
+    for (const auto& sh : shapes) {
+        const uint32_t ks = gemm_small_ksplit(sh[0], count, sh[1], sms);
+        if (ks > 1) wsf = std::max<uint64_t>(wsf, static_cast<uint64_t>(ks) * tt * nt * sh[0]);
+        tk = std::max<uint64_t>(tk, static_cast<uint64_t>(sh[0] / kGemmBN) * tt);
+    }
+    cudaStream_t s = m->ctx->stream;
+    if (wsf > b->gws_floats || tk > b->gtickets_n) {
+        VRT_CUDA(cudaStreamSynchronize(s));
+        if (wsf > b->gws_floats) {
+            cudaFree(b->gws);
+            b->gws = nullptr;
+            VRT_CUDA(cudaMalloc(&b->gws, std::max<uint64_t>(wsf, 1) * 4));
+            b->gws_floats = wsf;
+        }
+        if (tk > b->gtickets_n) {
+            cudaFree(b->gtickets);
+            b->gtickets = nullptr;
+            VRT_CUDA(cudaMalloc(&b->gtickets, tk * 4));
+            VRT_CUDA(cudaMemsetAsync(b->gtickets, 0, tk * 4, s));
+            b->gtickets_n = tk;
+        }
+    }
+    return VRT_OK;
+}
+
 // One decode step for sequences [0, count) on the model stream.
 static int batch_record_step(vrt_batch* b, uint32_t count) {
     vrt_model* m = b->m;
@@ -1407,7 +1446,17 @@ static int batch_record_step(vrt_batch* b, uint32_t count) {
         p.act_lo = al;
         p.ld_act = rows / 2;
         p.keys = b->keys;
-        VRT_CUDA(gemm_q8t(epi, hi, lo, p, s));
+        if (count > kGemmBM) {  // large-M kernel: 128-row token tiles, operands through the 128-row-box maps
+            const TmaMap& H = &hi == &b->xd_hi ? b->Xd_hi : &hi == &b->xq_hi ? b->Xq_hi : b->Xf_hi;
+            const TmaMap& Lo = &lo == &b->xd_lo ? b->Xd_lo : &lo == &b->xq_lo ? b->Xq_lo : b->Xf_lo;
+            VRT_CUDA(gemm_q8t(epi, H, Lo, p, s));
+            return VRT_OK;
+        }
+        p.nt = gemm_small_tile(count);
+        p.ksplit = gemm_small_ksplit(rows, count, k, m->ctx->prop.multiProcessorCount);
+        p.ws = b->gws;
+        p.tickets = b->gtickets;
+        VRT_CUDA(gemm_q8t_small(epi, hi, lo, p, s));
         return VRT_OK;
     };
     embed_rows_kernel<<<count, kRowThreads, 0, s>>>(m->arena + m->embd, b->tokens, c.vocab_size, d,
@@ -1474,6 +1523,8 @@ static void batch_free(vrt_batch* b) {
         cudaStreamSynchronize(b->m->ctx->stream);
     }
     if (b->graph) cudaGraphExecDestroy(b->graph);
+    cudaFree(b->gws);
+    cudaFree(b->gtickets);
     cudaFree(b->mem);
     delete b;
 }
@@ -2062,12 +2113,18 @@ int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, in
     if (!b->keep_logits) b->logits = nullptr;
     __half** hl[] = {&b->xh, &b->xl, &b->ah, &b->al};
     for (auto h : hl) *h = reinterpret_cast<__half*>(take());
-    VRT_TRY(make_f16_tmap(&b->xd_hi, b->xh, S, d));
-    VRT_TRY(make_f16_tmap(&b->xd_lo, b->xl, S, d));
-    VRT_TRY(make_f16_tmap(&b->xq_hi, b->xh, S, m->qwl));
-    VRT_TRY(make_f16_tmap(&b->xq_lo, b->xl, S, m->qwl));
-    VRT_TRY(make_f16_tmap(&b->xf_hi, b->ah, S, m->ffl));
-    VRT_TRY(make_f16_tmap(&b->xf_lo, b->al, S, m->ffl));
+    VRT_TRY(make_f16_tmap(&b->xd_hi, b->xh, S, d, 16));
+    VRT_TRY(make_f16_tmap(&b->xd_lo, b->xl, S, d, 16));
+    VRT_TRY(make_f16_tmap(&b->xq_hi, b->xh, S, m->qwl, 16));
+    VRT_TRY(make_f16_tmap(&b->xq_lo, b->xl, S, m->qwl, 16));
+    VRT_TRY(make_f16_tmap(&b->xf_hi, b->ah, S, m->ffl, 16));
+    VRT_TRY(make_f16_tmap(&b->xf_lo, b->al, S, m->ffl, 16));
+    VRT_TRY(make_f16_tmap(&b->Xd_hi, b->xh, S, d, 128));
+    VRT_TRY(make_f16_tmap(&b->Xd_lo, b->xl, S, d, 128));
+    VRT_TRY(make_f16_tmap(&b->Xq_hi, b->xh, S, m->qwl, 128));
+    VRT_TRY(make_f16_tmap(&b->Xq_lo, b->xl, S, m->qwl, 128));
+    VRT_TRY(make_f16_tmap(&b->Xf_hi, b->ah, S, m->ffl, 128));
+    VRT_TRY(make_f16_tmap(&b->Xf_lo, b->al, S, m->ffl, 128));
     b->host_pos.assign(max_seqs, 0);
     VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
     *out = b.release();
@@ -2131,6 +2188,7 @@ int vrt_batch_decode_steps(vrt_batch* b, uint32_t count, uint32_t steps) {
     vrt_model* m = b->m;
     cudaStream_t s = m->ctx->stream;
     VRT_CUDA(cudaSetDevice(m->ctx->device));
+    VRT_TRY(batch_gemm_workspace(b, count));
     if (m->opt.use_graph && (!b->graph || b->graph_count != count)) {
         if (b->graph) {
             VRT_CUDA(cudaStreamSynchronize(s));
