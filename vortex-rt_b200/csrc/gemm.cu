@@ -80,7 +80,7 @@ static cudaError_t gemm_small_launch_t(const TmaMap& hi, const TmaMap& lo, const
         done |= 1ull << dev;
     }
     const dim3 grid(p.n / kGemmBN, (p.m + p.nt - 1) / p.nt, p.ksplit);
-    return launch(q8t_gemm_small_kernel<EPI, NTMAX>, grid, dim3(kGemmThreads), smem, s, false, hi, lo, p);
+    return launch(q8t_gemm_small_kernel<EPI, NTMAX>, grid, dim3(kGemmSmallThreads), smem, s, false, hi, lo, p);
 }
 
 template <int NTMAX>
@@ -96,7 +96,8 @@ static cudaError_t gemm_small_epi(int epi, const TmaMap& hi, const TmaMap& lo, c
 cudaError_t gemm_q8t_small(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
     if (p.nt != 16 && p.nt != 32 && p.nt != 64 && p.nt != 128) return cudaErrorInvalidValue;
     if (p.ksplit == 0 || (p.ksplit > 1 && (!p.ws || !p.tickets))) return cudaErrorInvalidValue;
-    return p.nt <= 64 ? gemm_small_epi<64>(epi, hi, lo, p, s) : gemm_small_epi<128>(epi, hi, lo, p, s);
+    if (p.nt > 64) return cudaErrorInvalidValue;  // more rows: the large-M kernel
+    return gemm_small_epi<64>(epi, hi, lo, p, s);
 }
 
 // K splits for a small-M GEMM: enough CTAs for two per SM, at least two
@@ -109,7 +110,7 @@ uint32_t gemm_small_ksplit(uint32_t n, uint32_t m, uint32_t k, int sms) {
 }
 
 uint32_t gemm_small_tile(uint32_t m) {
-    return m <= 16 ? 16u : m <= 32 ? 32u : m <= 64 ? 64u : 128u;
+    return m <= 16 ? 16u : m <= 32 ? 32u : 64u;
 }
 
 cudaError_t gemm_q8t(int epi, const TmaMap& hi, const TmaMap& lo, const GemmParams& p, cudaStream_t s) {
@@ -169,7 +170,7 @@ static int gemm_common(vrt_ctx* ctx, int epi, const void* d_packed, uint32_t row
     VRT_CUDA(cudaSetDevice(ctx->device));
     const uint64_t xn = static_cast<uint64_t>(m) * cols;
     const uint64_t an = epi == kGemmGeluSplit ? static_cast<uint64_t>(m) * (rows / 2) : 0;
-    const bool small = m <= 128;  // weight rows on the MMA's 128 lanes, activation rows on N
+    const bool small = m <= 64;  // weight rows on the MMA's 128 lanes, activation rows on N
     const uint32_t nt = small ? gemm_small_tile(m) : 0u;
     const uint32_t ks = small ? gemm_small_ksplit(rows, m, cols, ctx->prop.multiProcessorCount) : 1u;
     const uint64_t ws_f = ks > 1 ? static_cast<uint64_t>(ks) * nt * rows : 0;   // partials (one token tile)
@@ -216,6 +217,7 @@ static int gemm_common(vrt_ctx* ctx, int epi, const void* d_packed, uint32_t row
 }  // namespace vrt
 
 using namespace vrt;
+
 
 extern "C" {
 

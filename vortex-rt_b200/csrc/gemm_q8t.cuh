@@ -57,6 +57,19 @@ constexpr int kGemmRawBytes = (kGemmBN / kTileRows) * kTileBytes;  // 17,408
 constexpr int kGemmThreads = 448;
 constexpr int kGemmEpiCols = 64;                              // accumulator columns per epilogue warp
 constexpr int kGemmChunkStages = 4;                           // operand stages (256 K columns) per accumulator chunk
+// Weight stages prefetched into L2 ahead of the shared-memory ring: a loaded
+// B200 answers a bulk copy from HBM in ~3.5 us, so ~140 KB per SM must be in
+// flight to stream at full rate; L2 holds that instead of shared memory.
+constexpr int kGemmL2Ahead = 8;
+
+// Prefetch raw stage `kt` (8 row groups' 2176-byte tiles, one 128-column K
+// tile) of a Q8T matrix whose row groups start at `wg` (KT tiles per group).
+__device__ __forceinline__ void prefetch_raw_stage(const uint8_t* wg, uint32_t KT, uint32_t kt) {
+#pragma unroll
+    for (int g = 0; g < kGemmBN / kTileRows; ++g) {
+        bulk_prefetch_l2(wg + (static_cast<uint64_t>(g) * KT + kt) * kTileBytes, kTileBytes);
+    }
+}
 constexpr uint32_t kGemmSmemBytes =
     1024 + kGemmStages * kGemmStageBytes + kGemmRawStages * kGemmRawBytes + 8 * (2 * kGemmStages + 2 * kGemmRawStages + 4) + 16;
 
@@ -148,8 +161,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: fp32 accumulate, fp16 A and B, both K-major, N = 128, M = 128.
+// Instruction descriptors: fp32 accumulate, fp16 A and B, both K-major, M = 128, N = 128 / 256.
 constexpr uint32_t kGemmIdesc = (1u << 4) | (static_cast<uint32_t>(kGemmBN >> 3) << 17) | (static_cast<uint32_t>(kGemmBM >> 4) << 24);
+constexpr uint32_t kGemmIdesc2 = (1u << 4) | (static_cast<uint32_t>((2 * kGemmBN) >> 3) << 17) | (static_cast<uint32_t>(kGemmBM >> 4) << 24);
 
 // Byte offset of element (row, col) (col < 64) in a 128-row K-major operand
 // tile with 128-byte rows and the 128B swizzle (16-byte chunk index XOR row % 8).
@@ -165,7 +179,14 @@ __host__ __device__ inline uint32_t sw128_offset(uint32_t row, uint32_t col) {
 // 1152 gives q exactly; hi = RN(q * s) (one HMUL2 of the exact product) and
 // lo = RN(q * s - hi) (one HFMA2) -- bit-identical to computing w = q * s in
 // fp32 (exact) and splitting it there.
+// PARTS threads share one (tile, lane) unit: thread t takes chunks
+// s = (4/PARTS)*(t % PARTS) .. of unit t / PARTS (PARTS = 1: 128 threads,
+// 2: 256 threads, each half the work).
+template <int PARTS = 1>
 __device__ __forceinline__ void dequant_half(const uint8_t* raw, int t, int h, uint8_t* whi, uint8_t* wlo) {
+    constexpr int SN = 4 / PARTS;
+    const int s0 = SN * (t % PARTS);
+    t /= PARTS;
     const int tile = t >> 4, i = t & 15;
     const int ln = 4 * (i >> 1) + 2 * h + (i & 1);  // Q8T lane: rows 2*(ln/4)+{0,1}, block ln % 4
     const uint8_t* src = raw + tile * kTileBytes;
@@ -175,7 +196,8 @@ __device__ __forceinline__ void dequant_half(const uint8_t* raw, int t, int h, u
     const __half2 bias = __float2half2_rn(1152.0f);
     const int kb = 32 * ((ln & 3) - 2 * h);  // 0 or 32 within the half
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
+    for (int ss = 0; ss < SN; ++ss) {
+        const int s = s0 + ss;
         const uint4 q = *reinterpret_cast<const uint4*>(src + (s * 32 + ln) * 16);
         const uint32_t row = tile * 16 + 2 * (ln >> 2) + (s >> 1);
         const uint32_t k0 = kb + 16 * (s & 1);
@@ -237,7 +259,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, 2 * kGemmBN);
+    // w_lo follows w_hi in the stage, so one B operand of 256 rows covers both:
+    // x_hi.[w_hi | w_lo] -> accumulator columns [0, 256), x_lo.w_hi adds into
+    // [0, 128); the epilogue adds the two column blocks.  Two accumulators of
+    // 256 columns fill TMEM.
+    if (warp == 1) tmem_alloc(tmem_slot, 4 * kGemmBN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -248,7 +274,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // ------------------------------------------------------- producer
         if (lane == 0) {
             const uint8_t* wg = p.w + static_cast<uint64_t>(n0 / kTileRows) * KT * kTileBytes;
+            for (uint32_t kt = 0; kt < KT && kt < static_cast<uint32_t>(kGemmL2Ahead); ++kt) prefetch_raw_stage(wg, KT, kt);
             for (uint32_t kt = 0; kt < KT; ++kt) {
+                if (kt + kGemmL2Ahead < KT) prefetch_raw_stage(wg, KT, kt + kGemmL2Ahead);
                 const uint32_t r = kt % kGemmRawStages;
                 if (kt >= kGemmRawStages) ok &= mbar_wait_bounded(&raw_empty[r], ((kt / kGemmRawStages) - 1) & 1);
                 mbar_arrive_expect_tx(&raw_full[r], kGemmRawBytes);
@@ -277,15 +305,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 ok &= mbar_wait_bounded(&full[s], (i / kGemmStages) & 1);
                 tc_fence_after();
                 const uint32_t base = smem_addr(ring + s * kGemmStageBytes);
-                const uint32_t acc = tmem + a * kGemmBN;
+                const uint32_t acc = tmem + a * 2 * kGemmBN;
 #pragma unroll
                 for (int kk = 0; kk < kGemmBK / 16; ++kk) {
                     const uint32_t o = kk * 32;  // 16 fp16 = 32 bytes along K inside the swizzle atom
                     const uint64_t ahi = sw128_desc(base + o), alo = sw128_desc(base + kGemmOpTile + o);
-                    const uint64_t bhi = sw128_desc(base + 2 * kGemmOpTile + o), blo = sw128_desc(base + 3 * kGemmOpTile + o);
-                    umma_f16(acc, ahi, bhi, kGemmIdesc, (first && kk == 0) ? 0u : 1u);
-                    umma_f16(acc, alo, bhi, kGemmIdesc, 1u);
-                    umma_f16(acc, ahi, blo, kGemmIdesc, 1u);
+                    const uint64_t bhl = sw128_desc(base + 2 * kGemmOpTile + o);  // w_hi rows then w_lo rows
+                    umma_f16(acc, ahi, bhl, kGemmIdesc2, (first && kk == 0) ? 0u : 1u);
+                    umma_f16(acc, alo, bhl, kGemmIdesc, 1u);
                 }
                 umma_commit(&empty[s]);
                 if ((i + 1) % kGemmChunkStages == 0 || i + 1 == NI) umma_commit(&acc_full[a]);
@@ -324,7 +351,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int c0 = 0; c0 < kGemmEpiCols; c0 += 32) {
                 uint32_t v[32];
-                tmem_ld32(tmem + ((32 * q) << 16) + a * kGemmBN + cb + c0, v);
+                tmem_ld32(tmem + ((32 * q) << 16) + a * 2 * kGemmBN + cb + c0, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum[c0 + j] = __fadd_rn(sum[c0 + j], __uint_as_float(v[j]));
+                tmem_ld32(tmem + ((32 * q) << 16) + a * 2 * kGemmBN + kGemmBN + cb + c0, v);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) sum[c0 + j] = __fadd_rn(sum[c0 + j], __uint_as_float(v[j]));
             }
@@ -398,7 +428,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * kGemmBN);
+        tmem_dealloc(tmem, 4 * kGemmBN);
     }
 }
 
@@ -419,27 +449,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // max of the 64-bit keys, one atomicMax per token and warp).
 template <int NTMAX>
 struct SmallGemmLayout {
+    static constexpr int kW = NTMAX <= 64 ? 4 : 3;                       // dequantised weight stages (w_hi, w_lo)
+    static constexpr int kWStage = 2 * kGemmOpTile;                      // 32 KB
+    static constexpr int kX = 2;                                         // activation stages (x_hi, x_lo)
     static constexpr int kXBytes = NTMAX * 128;                          // one activation operand tile
-    static constexpr int kStage = 2 * kXBytes + 2 * kGemmOpTile;         // x_hi, x_lo, w_hi, w_lo
-    static constexpr int kStages = 2;
-    static constexpr int kRaw =
-        (232448 - 1024 - kStages * kStage - 256) / kGemmRawBytes > 7 ? 7 : (232448 - 1024 - kStages * kStage - 256) / kGemmRawBytes;
-    static constexpr uint32_t kSmem = 1024 + kStages * kStage + kRaw * kGemmRawBytes + 8 * (2 * kStages + 2 * kRaw + 4) + 16;
+    static constexpr int kXStage = 2 * kXBytes;
+    static constexpr int kFree = 232448 - 1024 - 512 - kW * kWStage - kX * kXStage;
+    static constexpr int kRaw = kFree / kGemmRawBytes > 8 ? 8 : kFree / kGemmRawBytes;   // Q8T stages in flight
+    static constexpr uint32_t kBars = 8 * (2 * kW + 2 * kX + 2 * kRaw + 4);
+    static constexpr uint32_t kSmem = 1024 + kW * kWStage + kX * kXStage + kRaw * kGemmRawBytes + kBars + 16;
 };
 
+// warps: 0 weight stream, 1 MMA, 2-5 and 14-17 dequantisation, 6-13 epilogue,
+// 18 activation stream
+constexpr int kGemmSmallThreads = 608;
+
 template <int EPI, int NTMAX>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmSmallThreads, 1)
     q8t_gemm_small_kernel(const __grid_constant__ TmaMap x_hi, const __grid_constant__ TmaMap x_lo, const GemmParams p) {
     using LY = SmallGemmLayout<NTMAX>;
-    constexpr int S = LY::kStages, R = LY::kRaw;
+    constexpr int S = LY::kW, D = LY::kX, R = LY::kRaw;
     extern __shared__ uint8_t gsm_raw[];
     __shared__ uint32_t last_cta;
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* ring = sm;
-    uint8_t* raw = sm + S * LY::kStage;
-    uint64_t* full = reinterpret_cast<uint64_t*>(raw + R * kGemmRawBytes);
-    uint64_t* empty = full + S;
-    uint64_t* raw_full = empty + S;
+    uint8_t* wring = sm;
+    uint8_t* xring = wring + S * LY::kWStage;
+    uint8_t* raw = xring + D * LY::kXStage;
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(raw + R * kGemmRawBytes);
+    uint64_t* w_empty = w_full + S;
+    uint64_t* x_full = w_empty + S;
+    uint64_t* x_empty = x_full + D;
+    uint64_t* raw_full = x_empty + D;
     uint64_t* raw_empty = raw_full + R;
     uint64_t* acc_full = raw_empty + R;
     uint64_t* acc_empty = acc_full + 2;
@@ -452,17 +492,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t kt0 = KTALL * blockIdx.z / p.ksplit, kt1 = KTALL * (blockIdx.z + 1) / p.ksplit;
     const uint32_t KT = kt1 - kt0, NI = 2 * KT;
     const uint32_t NC = (NI + kGemmChunkStages - 1) / kGemmChunkStages;
-    const uint32_t tcols = NT < 16 ? 32u : 2u * NT;
-    const uint32_t idesc = (1u << 4) | ((NT >> 3) << 17) | (static_cast<uint32_t>(kGemmBN >> 4) << 24);
+    // x_lo sits right after x_hi's NT rows, so one B operand of 2*NT rows
+    // covers both: w_hi.[x_hi | x_lo] -> accumulator columns [0, 2NT), then
+    // w_lo.x_hi adds into [0, NT); the epilogue adds the two column blocks.
+    // Two MMAs per K step read each weight tile once.
+    const uint32_t tcols = 4u * NT;  // two accumulators of 2*NT columns
+    const uint32_t idesc2 = (1u << 4) | (((2 * NT) >> 3) << 17) | (static_cast<uint32_t>(kGemmBN >> 4) << 24);
+    const uint32_t idesc1 = (1u << 4) | ((NT >> 3) << 17) | (static_cast<uint32_t>(kGemmBN >> 4) << 24);
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1 + 4);  // activation expect_tx + 4 dequant warps
-            mbar_init(&empty[s], 1);
+            mbar_init(&w_full[s], 8);
+            mbar_init(&w_empty[s], 1);
+        }
+        for (int d = 0; d < D; ++d) {
+            mbar_init(&x_full[d], 1);
+            mbar_init(&x_empty[d], 1);
         }
         for (int r = 0; r < R; ++r) {
             mbar_init(&raw_full[r], 1);
-            mbar_init(&raw_empty[r], 4);
+            mbar_init(&raw_empty[r], 8);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
@@ -478,10 +527,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     bool ok = true;
 
     if (warp == 0) {
-        // weight stream only, up to R stages ahead of the dequantisation
+        // weight stream, up to R stages ahead of the dequantisation
         if (lane == 0) {
             const uint8_t* wg = p.w + static_cast<uint64_t>(n0 / kTileRows) * KTALL * kTileBytes;
+            for (uint32_t kt = 0; kt < KT && kt < static_cast<uint32_t>(kGemmL2Ahead); ++kt) {
+                prefetch_raw_stage(wg, KTALL, kt0 + kt);
+            }
             for (uint32_t kt = 0; kt < KT; ++kt) {
+                if (kt + kGemmL2Ahead < KT) prefetch_raw_stage(wg, KTALL, kt0 + kt + kGemmL2Ahead);
                 const uint32_t r = kt % R;
                 if (kt >= static_cast<uint32_t>(R)) ok &= mbar_wait_bounded(&raw_empty[r], ((kt / R) - 1) & 1);
                 mbar_arrive_expect_tx(&raw_full[r], kGemmRawBytes);
@@ -492,51 +545,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
         }
+    } else if (warp == 18) {
+        // activation tiles (16-row TMA boxes), up to D stages ahead of the MMAs
+        if (lane == 0) {
+            for (uint32_t i = 0; i < NI; ++i) {
+                const uint32_t d = i % D;
+                if (i >= static_cast<uint32_t>(D)) ok &= mbar_wait_bounded(&x_empty[d], ((i / D) - 1) & 1);
+                uint8_t* st = xring + d * LY::kXStage;
+                mbar_arrive_expect_tx(&x_full[d], 2 * NT * 128);
+                const int kx = static_cast<int>((kt0 + i / 2) * kTileCols + (i & 1) * kGemmBK);
+                for (uint32_t r0 = 0; r0 < NT; r0 += 16) {
+                    tma_load_2d(st + r0 * 128, &x_hi, kx, static_cast<int>(t0 + r0), &x_full[d]);
+                    tma_load_2d(st + (NT + r0) * 128, &x_lo, kx, static_cast<int>(t0 + r0), &x_full[d]);
+                }
+            }
+        }
     } else if (warp == 1) {
         if (lane == 0) {
             for (uint32_t i = 0; i < NI; ++i) {
                 const uint32_t c = i / kGemmChunkStages, a = c & 1, first = i % kGemmChunkStages == 0;
                 if (first && c >= 2) ok &= mbar_wait_bounded(&acc_empty[a], ((c / 2) - 1) & 1);
-                const uint32_t s = i % S;
-                ok &= mbar_wait_bounded(&full[s], (i / S) & 1);
+                const uint32_t s = i % S, d = i % D;
+                ok &= mbar_wait_bounded(&w_full[s], (i / S) & 1);
+                ok &= mbar_wait_bounded(&x_full[d], (i / D) & 1);
                 tc_fence_after();
-                const uint32_t base = smem_addr(ring + s * LY::kStage);
-                const uint32_t acc = tmem + a * NT;
+                const uint32_t wb = smem_addr(wring + s * LY::kWStage), xb = smem_addr(xring + d * LY::kXStage);
+                const uint32_t acc = tmem + a * 2 * NT;
 #pragma unroll
                 for (int kk = 0; kk < kGemmBK / 16; ++kk) {
                     const uint32_t o = kk * 32;
-                    const uint64_t xhi = sw128_desc(base + o), xlo = sw128_desc(base + LY::kXBytes + o);
-                    const uint64_t whi = sw128_desc(base + 2 * LY::kXBytes + o);
-                    const uint64_t wlo = sw128_desc(base + 2 * LY::kXBytes + kGemmOpTile + o);
-                    umma_f16(acc, whi, xhi, idesc, (first && kk == 0) ? 0u : 1u);
-                    umma_f16(acc, whi, xlo, idesc, 1u);
-                    umma_f16(acc, wlo, xhi, idesc, 1u);
+                    const uint64_t xhl = sw128_desc(xb + o);  // x_hi rows then x_lo rows
+                    const uint64_t whi = sw128_desc(wb + o), wlo = sw128_desc(wb + kGemmOpTile + o);
+                    umma_f16(acc, whi, xhl, idesc2, (first && kk == 0) ? 0u : 1u);
+                    umma_f16(acc, wlo, xhl, idesc1, 1u);
                 }
-                umma_commit(&empty[s]);
+                umma_commit(&w_empty[s]);
+                umma_commit(&x_empty[d]);
                 if ((i + 1) % kGemmChunkStages == 0 || i + 1 == NI) umma_commit(&acc_full[a]);
             }
         }
-    } else if (warp < 6) {
-        const int t = tid - 64;
+    } else if (warp < 6 || warp >= 14) {
+        const int t = warp < 6 ? tid - 64 : tid - 448 + 128;  // 0..255
         for (uint32_t kt = 0; kt < KT; ++kt) {
             const uint32_t r = kt % R;
             ok &= mbar_wait_bounded(&raw_full[r], (kt / R) & 1);
             for (int h = 0; h < 2; ++h) {
                 const uint32_t i = 2 * kt + h, s = i % S;
-                if (i >= static_cast<uint32_t>(S)) ok &= mbar_wait_bounded(&empty[s], ((i / S) - 1) & 1);
-                uint8_t* st = ring + s * LY::kStage;
-                if (t == 0) {  // this stage's activation tiles (16-row TMA boxes)
-                    mbar_arrive_expect_tx(&full[s], 2 * NT * 128);
-                    const int kx = static_cast<int>((kt0 + kt) * kTileCols + h * kGemmBK);
-                    for (uint32_t r0 = 0; r0 < NT; r0 += 16) {
-                        tma_load_2d(st + r0 * 128, &x_hi, kx, static_cast<int>(t0 + r0), &full[s]);
-                        tma_load_2d(st + LY::kXBytes + r0 * 128, &x_lo, kx, static_cast<int>(t0 + r0), &full[s]);
-                    }
-                }
-                dequant_half(raw + r * kGemmRawBytes, t, h, st + 2 * LY::kXBytes, st + 2 * LY::kXBytes + kGemmOpTile);
+                if (i >= static_cast<uint32_t>(S)) ok &= mbar_wait_bounded(&w_empty[s], ((i / S) - 1) & 1);
+                uint8_t* st = wring + s * LY::kWStage;
+                dequant_half<2>(raw + r * kGemmRawBytes, t, h, st, st + kGemmOpTile);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
+                if (lane == 0) mbar_arrive(&w_full[s]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_empty[r]);
@@ -557,10 +617,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j0 = 0; j0 < NTMAX / 2; j0 += 8) {
                 if (static_cast<uint32_t>(j0) < half_cols) {
-                    uint32_t v[8];
-                    tmem_ld8(tmem + ((32 * q) << 16) + a * NT + cb + j0, v);
+                    uint32_t v[8], u[8];
+                    tmem_ld8(tmem + ((32 * q) << 16) + a * 2 * NT + cb + j0, v);
+                    tmem_ld8(tmem + ((32 * q) << 16) + a * 2 * NT + NT + cb + j0, u);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) sum[j0 + e] = __fadd_rn(sum[j0 + e], __uint_as_float(v[e]));
+                    for (int e = 0; e < 8; ++e) {
+                        sum[j0 + e] = __fadd_rn(__fadd_rn(sum[j0 + e], __uint_as_float(v[e])), __uint_as_float(u[e]));
+                    }
                 }
             }
             tc_fence_before();

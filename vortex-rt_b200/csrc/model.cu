@@ -1396,7 +1396,7 @@ static int batch_gemm_workspace(vrt_batch* b, uint32_t count) {
     const int sms = m->ctx->prop.multiProcessorCount;
     const uint32_t d = c.embedding_length;
     const uint32_t shapes[][2] = {{m->qwl + 2 * m->kwl, d}, {d, m->qwl}, {2 * m->ffl, d}, {d, m->ffl}, {c.vocab_size, d}};
-    if (count > kGemmBM) return VRT_OK;  // large-M kernel: no split-K workspace
+    if (count > 64) return VRT_OK;  // large-M kernel: no split-K workspace
     const uint32_t nt = gemm_small_tile(count), tt = (count + nt - 1) / nt;
     uint64_t wsf = 0, tk = 0;
     for (const auto& sh : shapes) {
@@ -1446,7 +1446,7 @@ static int batch_record_step(vrt_batch* b, uint32_t count) {
         p.act_lo = al;
         p.ld_act = rows / 2;
         p.keys = b->keys;
-        if (count > kGemmBM) {  // large-M kernel: 128-row token tiles, operands through the 128-row-box maps
+        if (count > 64) {  // large-M kernel: 128-row token tiles, operands through the 128-row-box maps
             const TmaMap& H = &hi == &b->xd_hi ? b->Xd_hi : &hi == &b->xq_hi ? b->Xq_hi : b->Xf_hi;
             const TmaMap& Lo = &lo == &b->xd_lo ? b->Xd_lo : &lo == &b->xq_lo ? b->Xq_lo : b->Xf_lo;
             VRT_CUDA(gemm_q8t(epi, H, Lo, p, s));
