@@ -45,6 +45,12 @@ def test_tp4_peer_matches_single_gpu():
     run_worker("27b-slice", "peer", 4)
 
 
+@pytest.mark.skipif(gpus() < 8, reason="needs 8 GPUs")
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+def test_tp8_matches_single_gpu(mode):
+    run_worker("27b-slice", mode, 8)
+
+
 @pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
 def test_tp2_peer_wait_times_out():
     run_worker("tiny-gqa", "peer-timeout")
