@@ -196,8 +196,10 @@ def run_reference_arm(args, rank: int, world: int):
 
 def run_batched(args, rank: int, world: int, local: int):
     """Configs 3 / 4-bs32: independent sequences decoded together (vrt_batch).
-    Under torchrun the sequences are split evenly over the ranks, each rank a
-    full replica with no collective on the data path ("replicas")."""
+    Under torchrun, config 3 splits the sequences evenly over the ranks, each
+    rank a full replica with no collective on the data path ("replicas");
+    config 4 at batch 32 is tensor parallel (every rank holds all sequences
+    and 1/N of every projection, NCCL all-reduce after o-proj and down)."""
     import datetime
 
     import torch
@@ -209,20 +211,25 @@ def run_batched(args, rank: int, world: int, local: int):
     if dist_on:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
-    if args.workload == "27b-bs32" and world > 1:
-        raise SystemExit("27b-bs32 runs on one GPU (batched decode under tensor parallelism is not built)")
+    tp = args.workload == "27b-bs32" and world > 1
     shape = shape_for(args.workload)
     if args.layers:
         shape = shape.with_(block_count=args.layers)
     if args.vocab:
         shape = shape.with_(vocab_size=args.vocab)
     total = BATCH_SEQS[args.workload]
-    M = total // world
+    M = total if tp else total // world
     prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
     e2e_steps = max(4, args.steps // 4)
     P = prompt_len + args.warmup + args.steps + e2e_steps + 8
+    nccl_id = None
+    if tp:
+        obj = [vrt.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
     ctx = vrt.Context(local)
-    model = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=1234, max_positions=P)
+    model = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=1234, max_positions=P,
+                      tp_rank=rank if tp else 0, tp_world=world if tp else 1, nccl_id=nccl_id)
     b = vrt.Batch(model, M, P)
     stream = torch.cuda.ExternalStream(ctx.stream)
 
@@ -236,7 +243,7 @@ def run_batched(args, rank: int, world: int, local: int):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    rng = np.random.default_rng(3 + rank)
+    rng = np.random.default_rng(3 if tp else 3 + rank)  # tensor parallel: the same prompts on every rank
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     barrier()
     ev[0].record(stream)
@@ -280,6 +287,8 @@ def run_batched(args, rank: int, world: int, local: int):
         mid = prompt_len + args.warmup + args.steps // 2
         weights = bytes_per_token(shape, 0)  # weights + norms (+ one position of KV)
         step_bytes = weights + M * (bytes_per_token(shape, mid) - weights)
+        if tp:
+            step_bytes /= world  # per GPU: weights and KV heads are both sharded
         achieved = step_bytes / (ms / 1000.0 / args.steps) / 1e9
         cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, os.cpu_count() or 1)
         line = {
@@ -291,10 +300,11 @@ def run_batched(args, rank: int, world: int, local: int):
                                                   f"{prompt_len}-token prompts, greedy decode, sequences split over "
                                                   f"{world} replica(s)",
                                     "27b-bs32": f"config 4 at batch {total}: 27B-shaped, {prompt_len}-token prompts"
+                                                + (f", tensor parallel over {world} GPUs" if tp else "")
                                     }[args.workload],
                        "d_model": shape.embedding_length, "layers": shape.block_count, "vocab": shape.vocab_size,
                        "global_batch": total, "sequences_per_gpu": M,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1 else "single GPU",
                        "positions": f"{prompt_len + args.warmup}..{prompt_len + args.warmup + args.steps}",
                        "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB per step)"},
             "gpu_launches": (7 * shape.block_count + 3) * args.steps,

@@ -243,13 +243,17 @@ VRT_API int vrt_model_reset(vrt_model* m);
 
 /* Gemma3Model::decode_token (src/gemma3.cpp:1462-1882).  position must equal
  * the next position.  top_k == 0 skips the LM head; 1 = fused LM head +
- * argmax; >1 = full logits, top-k by value.  h_hidden (optional) receives the
- * final normed hidden state (embedding_length floats); h_ids/h_logits receive
- * min(top_k, vocab) entries. */
+ * argmax; >1 = full logits, top-k by value (ties -> lower id).  h_hidden
+ * (optional) receives the final normed hidden state (embedding_length
+ * floats); h_ids/h_logits receive min(top_k, vocab) entries.  Under tensor
+ * parallelism every rank makes the same call; with top_k > 1 the ranks'
+ * logits shards are all-gathered and every rank returns the same top-k. */
 VRT_API int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t top_k,
                             float* h_hidden, uint32_t* h_ids, float* h_logits);
 
-/* Full-vocabulary logits of the last decode step into h_logits (vocab floats). */
+/* Full-vocabulary logits of the last decode step into h_logits (vocab
+ * floats).  Under tensor parallelism it gathers every rank's shard: all ranks
+ * must call it together. */
 VRT_API int vrt_model_logits(vrt_model* m, float* h_logits);
 
 /* Gemma3Model::generate_greedy_tokens (src/gemma3.cpp:2080-2149): token-by-token

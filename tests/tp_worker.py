@@ -7,6 +7,13 @@ Modes:
                   seeded model unsharded (TP=1) and compares hidden states and
                   greedy ids.  With the peer exchange every rank must also
                   hold bit-identical hidden states (ranks sum in one order).
+                  Then a top_k = 8 step and the full logits (gathered from
+                  all ranks' vocabulary shards) against TP=1.
+  batch        -- batched decode (vrt_batch) under tensor parallelism: four
+                  sequences prefilled (tensor-core prefill with NCCL sums) and
+                  decoded together; ids and per-sequence logits (gathered
+                  from the ranks' vocabulary shards) against a single-GPU
+                  batch of the same seeded model.
   peer-timeout -- failure detection without a GPU fault: after two joint
                   steps rank 1 sits out one step (between steps, nothing in
                   flight); rank 0's exchange waits run out after 1 s and its
@@ -55,6 +62,64 @@ def compare_with_single_gpu(ctx, cfg, seed, toks, steps, hs, gen, world):
     return ok
 
 
+def compare_top_k(ctx, cfg, seed, toks, ids8, lg8, full):
+    """TP top-8 and full logits against TP=1: logits within 1e-3 abs + rel;
+    ids equal except where TP=1 neighbours in the sorted order are within
+    1e-3 (a near-tie may swap)."""
+    ref = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64)
+    for p, t in enumerate(toks[:-1]):
+        ref.decode(t, p, 1)
+    _, ids_r, lg_r = ref.decode(toks[-1], len(toks) - 1, 8)
+    full_r = ref.logits()
+    ref.close()
+    bound = 1e-3 + 1e-3 * np.abs(full_r.astype(np.float64))
+    err = float(np.max(np.abs(full.astype(np.float64) - full_r) / bound))
+    ok = err <= 1.0 and bool(np.all(np.abs(lg8.astype(np.float64) - lg_r) <= 1e-3 + 1e-3 * np.abs(lg_r)))
+    srt = np.sort(full_r)[::-1][:9]
+    for i, (a, b) in enumerate(zip(ids8, ids_r)):
+        if a != b:
+            near = (i > 0 and srt[i - 1] - srt[i] < 1e-3) or srt[i] - srt[i + 1] < 1e-3
+            ok = ok and near
+    print(f"top-8 vs TP1: ids {list(ids8)} / {list(ids_r)}; full logits worst err/bound {err:.3g}; ok {ok}",
+          flush=True)
+    return ok
+
+
+def run_batch(ctx, m, cfg, seed, shape, steps, rank, world):
+    rng = np.random.default_rng(seed + 1)
+    prompts = [[2] + rng.integers(3, shape.vocab_size, n).tolist() for n in (5, 9, 3, 12)]
+
+    def decode(model):
+        b = vrt.Batch(model, 4, 64, keep_logits=True)
+        for i, pr in enumerate(prompts):
+            b.prefill(i, pr)
+        b.decode_steps(4, steps)
+        ids = [b.read(i)[0] for i in range(4)]
+        lg = [b.logits(i) for i in range(4)]
+        b.close()
+        return ids, lg
+
+    ids, lg = decode(m)
+    mine = torch.tensor(np.concatenate([np.asarray(x, np.int64) for x in ids]), device="cuda")
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    ok = all(torch.equal(every[0], x) for x in every[1:])
+    if rank == 0:
+        ref = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64)
+        ids_r, lg_r = decode(ref)
+        ref.close()
+        err = max(float(np.max(np.abs(a.astype(np.float64) - b) / (1e-3 + 1e-3 * np.abs(b)))) for a, b in zip(lg, lg_r))
+        same = ids == ids_r
+        print(f"batch TP{world}: ids identical on all ranks {ok}; ids equal to TP1 {same}; "
+              f"last-step logits worst err/bound {err:.3g}", flush=True)
+        if not same:
+            for a, b in zip(ids, ids_r):
+                if a != b:
+                    print(f"  TP{world} {a}\n  TP1 {b}", flush=True)
+        ok = ok and same and err <= 1.0
+    return ok
+
+
 def main():
     shape_name, seed, steps = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
     mode = sys.argv[4] if len(sys.argv) > 4 else "peer"
@@ -71,7 +136,9 @@ def main():
                   nccl_id=obj[0], tp_exchange=exchange, tp_wait_ms=1000 if mode == "peer-timeout" else 0)
     toks = [2] + np.random.default_rng(seed).integers(3, shape.vocab_size, 7).tolist()
     ok = True
-    if mode == "peer-timeout":
+    if mode == "batch":
+        ok = run_batch(ctx, m, cfg, seed, shape, steps, rank, world)
+    elif mode == "peer-timeout":
         for p, t in enumerate(toks[:2]):
             m.decode(t, p, 1)
         dist.barrier()
@@ -101,8 +168,20 @@ def main():
             if rank == 0:
                 print(f"hidden states identical on all ranks: {same}", flush=True)
             ok = same
+        # top-k (> 1) and the full logits: every rank gathers all shards
+        m.reset()
+        for p, t in enumerate(toks[:-1]):
+            m.decode(t, p, 1)
+        _, ids8, lg8 = m.decode(toks[-1], len(toks) - 1, 8)
+        full = m.logits()
+        mine = torch.tensor(ids8.astype(np.int64), device="cuda")
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        same_k = all(torch.equal(every[0], x) for x in every[1:])
         if rank == 0:
-            ok = compare_with_single_gpu(ctx, cfg, seed, toks, steps, hs, gen, world) and ok
+            print(f"top-8 ids identical on all ranks: {same_k}", flush=True)
+            ok = compare_with_single_gpu(ctx, cfg, seed, toks, steps, hs, gen, world) and ok and same_k
+            ok = compare_top_k(ctx, cfg, seed, toks, ids8, lg8, full) and ok
     m.close()
     flag = torch.tensor([1 if ok else 0], device="cuda")
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)

@@ -306,6 +306,7 @@ struct vrt_model {
     unsigned long long** tp_peers_dev = nullptr;        // the same table on the device
     float* tp_sum = nullptr;                            // reduced vectors, [2][d]
     uint32_t* tp_bar = nullptr;                         // grid barrier counter, generation
+    float* logits_full = nullptr;                       // tensor parallel: all ranks' logits shards, [vocab]
     // batched prefill buffers, [chunk][...] rows (allocated at the first batched prefill)
     struct Prefill {
         uint32_t cap = 0;
@@ -774,6 +775,15 @@ static int nccl_sum(vrt_model* m, float* buf, size_t n, cudaStream_t s) {
     return VRT_OK;
 }
 
+// Tensor parallelism, batched paths: the per-row argmax keys (64-bit,
+// value-ordered) maximised over the ranks' vocabulary shards.
+static int nccl_key_max(vrt_model* m, unsigned long long* keys, size_t n, cudaStream_t s) {
+    if (m->world <= 1) return VRT_OK;
+    const int r = m->nccl.AllReduce(keys, keys, n, /*ncclUint64*/ 5, /*ncclMax*/ 2, m->comm, s);
+    if (r) return fail(VRT_E_CUDA, "ncclAllReduce(max) failed: %s", m->nccl.GetErrorString(r));
+    return VRT_OK;
+}
+
 // Exchange parameters of one consumer of row-parallel partial sums.  Ops are
 // numbered per step: 2l = attention output of layer l (slot set 0), 2l+1 =
 // FFN down of layer l (set 1), 2L = the argmax key.
@@ -1119,6 +1129,7 @@ static void destroy_model(vrt_model* m) {
     cudaFree(m->prompt);
     cudaFree(m->st);
     cudaFree(m->key_tmp);
+    cudaFree(m->logits_full);
     cudaFree(m->pf.mem);
     if (m->st_host) cudaFreeHost(m->st_host);
     if (m->hidden_host) cudaFreeHost(m->hidden_host);
@@ -1339,11 +1350,13 @@ static int prefill_layers(vrt_model* m, const SeqTarget& t, uint32_t n) {
             kv_store_kernel<<<dim3(nc, m->KVl), 128, 0, s>>>(B.k, B.v, t.kc[l], t.vc[l], t.cap[l], m->KVl, hd, p0, nc);
             VRT_CUDA(cudaGetLastError());
             VRT_TRY(gemm(kGemmStore, B.xq_hi, B.xq_lo, m->arena + L.o, d, m->qwl, nc, B.o, nullptr, nullptr));
+            VRT_TRY(nccl_sum(m, B.o, static_cast<size_t>(nc) * d, s));  // row-parallel partials (tensor parallel)
             resid_rows_kernel<<<nc, kRowThreads, 0, s>>>(B.o, B.h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
                                                         B.h1, B.xh, B.xl, status);
             VRT_CUDA(cudaGetLastError());
             VRT_TRY(gemm(kGemmGeluSplit, B.xd_hi, B.xd_lo, m->arena + L.gu, 2 * m->ffl, d, nc, nullptr, B.ah, B.al));
             VRT_TRY(gemm(kGemmStore, B.xf_hi, B.xf_lo, m->arena + L.down, d, m->ffl, nc, B.dn, nullptr, nullptr));
+            VRT_TRY(nccl_sum(m, B.dn, static_cast<size_t>(nc) * d, s));
         }
     }
     // last prompt token: final residual + output norm -> tied LM head + argmax
@@ -1364,6 +1377,7 @@ static int prefill_layers(vrt_model* m, const SeqTarget& t, uint32_t n) {
     p.status = status;
     p.eps = c.rms_epsilon;
     VRT_CUDA(gemv_q8t(kProResidFinal, kEpiArgmax, p, gemv_grid(m->ctx->prop.multiProcessorCount, p.rows), s, false));
+    VRT_TRY(nccl_key_max(m, t.key, 1, s));
     return VRT_OK;
 }
 
@@ -1379,7 +1393,7 @@ static int prefill_batched(vrt_model* m, uint32_t n) {
 // --------------------------------------------------------- batched decode
 
 static bool batch_supported(const vrt_model* m) {
-    return m->world <= 1 && prefill_supported(m) && m->cfg.vocab_size % kGemmBN == 0;
+    return prefill_supported(m) && (m->vocab_hi - m->vocab_lo) % kGemmBN == 0;
 }
 
 static uint32_t batch_splits(const vrt_batch* b, uint32_t count, uint32_t cap) {
@@ -1395,7 +1409,8 @@ static int batch_gemm_workspace(vrt_batch* b, uint32_t count) {
     const auto& c = m->cfg;
     const int sms = m->ctx->prop.multiProcessorCount;
     const uint32_t d = c.embedding_length;
-    const uint32_t shapes[][2] = {{m->qwl + 2 * m->kwl, d}, {d, m->qwl}, {2 * m->ffl, d}, {d, m->ffl}, {c.vocab_size, d}};
+    const uint32_t shapes[][2] = {{m->qwl + 2 * m->kwl, d}, {d, m->qwl}, {2 * m->ffl, d}, {d, m->ffl},
+                                  {m->vocab_hi - m->vocab_lo, d}};
     if (count > 64) return VRT_OK;  // large-M kernel: no split-K workspace
     const uint32_t nt = gemm_small_tile(count), tt = (count + nt - 1) / nt;
     uint64_t wsf = 0, tk = 0;
@@ -1441,11 +1456,12 @@ static int batch_record_step(vrt_batch* b, uint32_t count) {
         p.m = count;
         p.status = status;
         p.y = y;
-        p.ldy = rows;
+        p.ldy = epi == kGemmArgmax ? c.vocab_size : rows;
         p.act_hi = ah;
         p.act_lo = al;
         p.ld_act = rows / 2;
         p.keys = b->keys;
+        p.row_base = epi == kGemmArgmax ? m->vocab_lo : 0u;
         if (count > 64) {  // large-M kernel: 128-row token tiles, operands through the 128-row-box maps
             const TmaMap& H = &hi == &b->xd_hi ? b->Xd_hi : &hi == &b->xq_hi ? b->Xq_hi : b->Xf_hi;
             const TmaMap& Lo = &lo == &b->xd_lo ? b->Xd_lo : &lo == &b->xq_lo ? b->Xq_lo : b->Xf_lo;
@@ -1498,18 +1514,25 @@ static int batch_record_step(vrt_batch* b, uint32_t count) {
         a.out_lo = b->xl;
         VRT_CUDA(attention_launch(a, dim3(a.splits, m->KVl, count), s, false));
         VRT_TRY(gemm(kGemmStore, b->xq_hi, b->xq_lo, m->arena + L.o, d, m->qwl, b->o, nullptr, nullptr));
+        VRT_TRY(nccl_sum(m, b->o, static_cast<size_t>(count) * d, s));  // row-parallel partials (tensor parallel)
         resid_rows_kernel<<<count, kRowThreads, 0, s>>>(b->o, b->h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
                                                        b->h1, b->xh, b->xl, status);
         VRT_CUDA(cudaGetLastError());
         VRT_TRY(gemm(kGemmGeluSplit, b->xd_hi, b->xd_lo, m->arena + L.gu, 2 * m->ffl, d, nullptr, b->ah, b->al));
         VRT_TRY(gemm(kGemmStore, b->xf_hi, b->xf_lo, m->arena + L.down, d, m->ffl, b->dn, nullptr, nullptr));
+        VRT_TRY(nccl_sum(m, b->dn, static_cast<size_t>(count) * d, s));
     }
     const auto& lastL = m->layers[c.block_count - 1];
     final_rows_kernel<<<count, kRowThreads, 0, s>>>(b->dn, b->h1, F(lastL.n_post_ffw), F(m->out_norm), c.rms_epsilon, d,
                                                    b->hidden, b->xh, b->xl, status);
     VRT_CUDA(cudaGetLastError());
-    VRT_TRY(gemm(kGemmArgmax, b->xd_hi, b->xd_lo, m->arena + m->embd, c.vocab_size, d,
-                 b->keep_logits ? b->logits : nullptr, nullptr, nullptr));
+    // tied LM head over this rank's vocabulary rows; logits rows keep the
+    // full-vocabulary stride (this rank's columns at vocab_lo)
+    const uint32_t kt = d / kTileCols, vl = m->vocab_hi - m->vocab_lo;
+    VRT_TRY(gemm(kGemmArgmax, b->xd_hi, b->xd_lo,
+                 m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes, vl, d,
+                 b->keep_logits ? b->logits + m->vocab_lo : nullptr, nullptr, nullptr));
+    VRT_TRY(nccl_key_max(m, b->keys, count, s));
     batch_finalize_kernel<<<(count + 127) / 128, 128, 0, s>>>(b->keys, b->tokens, b->pos, b->out_ids, b->out_count,
                                                              b->out_cap, 0, count, c.vocab_size, 0, status);
     VRT_CUDA(cudaGetLastError());
@@ -1630,6 +1653,19 @@ int vrt_model_reset(vrt_model* m) {
     return VRT_OK;
 }
 
+// Tensor parallelism: every rank's logits shard into m->logits_full (the
+// vocabulary in order; shards are equal and contiguous) by one in-place NCCL
+// all-gather on the model's communicator.  Collective: every rank calls it.
+static int gather_logits(vrt_model* m, cudaStream_t s) {
+    const uint32_t vl = m->vocab_hi - m->vocab_lo;
+    if (!m->logits_full) VRT_CUDA(cudaMalloc(&m->logits_full, 4ull * m->cfg.vocab_size));
+    float* mine = m->logits_full + m->vocab_lo;
+    VRT_CUDA(cudaMemcpyAsync(mine, m->logits, 4ull * vl, cudaMemcpyDeviceToDevice, s));
+    const int r = m->nccl.AllGather(mine, m->logits_full, vl, /*ncclFloat32*/ 7, m->comm, s);
+    if (r) return fail(VRT_E_CUDA, "ncclAllGather(logits) failed: %s", m->nccl.GetErrorString(r));
+    return VRT_OK;
+}
+
 int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t top_k, float* h_hidden,
                     uint32_t* h_ids, float* h_logits) {
     clear_error();
@@ -1642,7 +1678,6 @@ int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t to
         vrt_model_reset(m);
         return fail(VRT_E_INVALID, "Token id is outside Gemma 3 vocabulary");
     }
-    if (top_k > 1 && m->world > 1) return fail(VRT_E_UNSUPPORTED, "top_k > 1 is not available with tensor parallelism");
     cudaStream_t s = m->ctx->stream;
     VRT_CUDA(cudaSetDevice(m->ctx->device));
     StepState* sh = m->st_host;
@@ -1652,12 +1687,16 @@ int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t to
     sh->prompt_count = 0;
     VRT_CUDA(cudaMemcpyAsync(m->st, sh, 20, cudaMemcpyHostToDevice, s));
     VRT_TRY(run_step(m, top_k > 0));
+    // top_k > 1 under tensor parallelism: gather the logits shards (every
+    // rank makes the same call, as for the step itself)
+    if (top_k > 1 && m->world > 1) VRT_TRY(gather_logits(m, s));
     VRT_CUDA(cudaMemcpyAsync(sh, m->st, kStepStateHostBytes, cudaMemcpyDeviceToHost, s));
     if (h_hidden) VRT_CUDA(cudaMemcpyAsync(m->hidden_host, m->hidden, 4ull * c.embedding_length, cudaMemcpyDeviceToHost, s));
     std::vector<float> logits;
     if (top_k > 1) {
         logits.resize(c.vocab_size);
-        VRT_CUDA(cudaMemcpyAsync(logits.data(), m->logits, 4ull * c.vocab_size, cudaMemcpyDeviceToHost, s));
+        VRT_CUDA(cudaMemcpyAsync(logits.data(), m->world > 1 ? m->logits_full : m->logits, 4ull * c.vocab_size,
+                                 cudaMemcpyDeviceToHost, s));
     }
     VRT_CUDA(cudaStreamSynchronize(s));
     uint32_t status;
@@ -1694,9 +1733,14 @@ int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t to
 }
 
 int vrt_model_logits(vrt_model* m, float* h_logits) {
+    clear_error();
     if (!m || !h_logits) return fail(VRT_E_INVALID, "null argument");
-    const uint32_t n = m->vocab_hi - m->vocab_lo;
-    VRT_CUDA(cudaMemcpy(h_logits, m->logits, 4ull * n, cudaMemcpyDeviceToHost));
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    cudaStream_t s = m->ctx->stream;
+    if (m->world > 1) VRT_TRY(gather_logits(m, s));
+    VRT_CUDA(cudaMemcpyAsync(h_logits, m->world > 1 ? m->logits_full : m->logits, 4ull * m->cfg.vocab_size,
+                             cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaStreamSynchronize(s));
     return VRT_OK;
 }
 
@@ -1715,7 +1759,7 @@ int vrt_prefill(vrt_model* m, const uint32_t* h_prompt, uint32_t n) {
     VRT_CUDA(cudaMemcpyAsync(m->prompt, h_prompt, 4ull * n, cudaMemcpyHostToDevice, s));
     StepState* sh = m->st_host;
     memset(sh, 0, kStepStateHostBytes);
-    const bool batched = m->world <= 1 && !m->trace_on && m->opt.prefill_chunk != 1 && n >= 2 && prefill_supported(m);
+    const bool batched = !m->trace_on && m->opt.prefill_chunk != 1 && n >= 2 && prefill_supported(m);
     sh->token = batched ? h_prompt[n - 1] : h_prompt[0];
     sh->pos = batched ? n - 1 : 0;  // the batched pass leaves only the last token's LM head + finalize
     sh->prompt_count = n;
@@ -2054,8 +2098,8 @@ int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, in
     if (!m || !out) return fail(VRT_E_INVALID, "null argument");
     *out = nullptr;
     if (!batch_supported(m)) {
-        return fail(VRT_E_UNSUPPORTED, "batched decode needs one GPU (tp_world <= 1), 128-multiple projection widths, "
-                                       "1/2/4/8 query heads per KV head and a 128-multiple vocabulary");
+        return fail(VRT_E_UNSUPPORTED, "batched decode needs 128-multiple projection widths per rank, "
+                                       "1/2/4/8 query heads per KV head and a 128-multiple vocabulary shard");
     }
     if (max_seqs == 0 || max_seqs > 4096) return fail(VRT_E_INVALID, "max_seqs must be 1..4096");
     if (max_positions == 0 || max_positions > m->P) {
@@ -2163,7 +2207,7 @@ int vrt_batch_prefill(vrt_batch* b, uint32_t seq, const uint32_t* h_prompt, uint
     t.positions = b->P;
     t.key = b->keys + seq;
     t.hidden = b->hidden + static_cast<uint64_t>(seq) * c.embedding_length;
-    t.logits = b->keep_logits ? b->logits + static_cast<uint64_t>(seq) * c.vocab_size : nullptr;
+    t.logits = b->keep_logits ? b->logits + static_cast<uint64_t>(seq) * c.vocab_size + m->vocab_lo : nullptr;
     VRT_CUDA(cudaMemsetAsync(t.key, 0, 8, s));
     VRT_TRY(prefill_layers(m, t, n));
     batch_finalize_kernel<<<1, 1, 0, s>>>(b->keys, b->tokens, b->pos, b->out_ids, b->out_count, b->out_cap, seq, 1,
@@ -2258,10 +2302,17 @@ int vrt_batch_logits(vrt_batch* b, uint32_t seq, float* h_logits) {
     if (!b || !h_logits) return fail(VRT_E_INVALID, "null argument");
     if (!b->keep_logits) return fail(VRT_E_STATE, "batch created without keep_logits");
     if (seq >= b->S) return fail(VRT_E_INVALID, "sequence %u outside the batch of %u", seq, b->S);
-    const uint32_t V = b->m->cfg.vocab_size;
-    VRT_CUDA(cudaSetDevice(b->m->ctx->device));
-    VRT_CUDA(cudaStreamSynchronize(b->m->ctx->stream));
-    VRT_CUDA(cudaMemcpy(h_logits, b->logits + static_cast<uint64_t>(seq) * V, 4ull * V, cudaMemcpyDeviceToHost));
+    vrt_model* m = b->m;
+    const uint32_t V = m->cfg.vocab_size, vl = m->vocab_hi - m->vocab_lo;
+    cudaStream_t s = m->ctx->stream;
+    VRT_CUDA(cudaSetDevice(m->ctx->device));
+    float* row = b->logits + static_cast<uint64_t>(seq) * V;
+    if (m->world > 1) {  // every rank holds its vocabulary columns: gather them (collective)
+        const int r = m->nccl.AllGather(row + m->vocab_lo, row, vl, /*ncclFloat32*/ 7, m->comm, s);
+        if (r) return fail(VRT_E_CUDA, "ncclAllGather(logits) failed: %s", m->nccl.GetErrorString(r));
+    }
+    VRT_CUDA(cudaMemcpyAsync(h_logits, row, 4ull * V, cudaMemcpyDeviceToHost, s));
+    VRT_CUDA(cudaStreamSynchronize(s));
     return VRT_OK;
 }
 
