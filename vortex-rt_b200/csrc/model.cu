@@ -34,6 +34,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "prefill.cuh"
@@ -582,18 +583,43 @@ static int alloc_runtime(vrt_model* m) {
 
 // ------------------------------------------------------- weight loading
 
+// Streaming Q8_0 upload: the GGUF file is memory-mapped; row runs are copied
+// into one of kLoadBufs pinned staging buffers by host worker threads, then
+// uploaded and repacked into the Q8T layout on the device stream.  A buffer
+// is refilled only after the CUDA event recorded behind its repack has
+// completed, so the host copy of chunk k+1 overlaps the upload and repack of
+// chunk k (the reference uploads 32 MiB chunks synchronously,
+// src/gemma3.cpp:571-600).
 struct Loader {
+    static constexpr int kLoadBufs = 3;
     vrt_model* m;
-    uint8_t* h_stage = nullptr;  // pinned
-    uint8_t* d_stage = nullptr;
-    uint64_t cap = 64ull << 20;
+    uint8_t* h_stage[kLoadBufs] = {};  // pinned
+    uint8_t* d_stage[kLoadBufs] = {};
+    cudaEvent_t done[kLoadBufs] = {};
+    bool used[kLoadBufs] = {};
+    int next = 0;
+    uint64_t cap = 32ull << 20;
+    unsigned workers = 1;
     ~Loader() {
-        if (h_stage) cudaFreeHost(h_stage);
-        if (d_stage) cudaFree(d_stage);
+        if (m) cudaStreamSynchronize(m->ctx->stream);
+        for (int i = 0; i < kLoadBufs; ++i) {
+            if (h_stage[i]) cudaFreeHost(h_stage[i]);
+            if (d_stage[i]) cudaFree(d_stage[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
     }
     int init() {
-        VRT_CUDA(cudaMallocHost(&h_stage, cap));
-        VRT_CUDA(cudaMalloc(&d_stage, cap));
+        for (int i = 0; i < kLoadBufs; ++i) {
+            VRT_CUDA(cudaMallocHost(&h_stage[i], cap));
+            VRT_CUDA(cudaMalloc(&d_stage[i], cap));
+            VRT_CUDA(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming));
+        }
+        workers = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+        return VRT_OK;
+    }
+    // all queued uploads and repacks finished
+    int finish() {
+        VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
         return VRT_OK;
     }
     // rows [r0, r0+nr) x blocks [b0, b0+nb) of a raw Q8_0 tensor -> Q8T destination
@@ -606,11 +632,27 @@ struct Loader {
         cudaStream_t s = m->ctx->stream;
         for (uint32_t r = 0; r < nr; r += rows_per) {
             const uint32_t n = std::min(rows_per, nr - r);
-            for (uint32_t i = 0; i < n; ++i) {
-                memcpy(h_stage + i * take, src + (static_cast<uint64_t>(r0 + r + i)) * src_row_bytes + b0 * 34ull, take);
+            const int k = next;
+            next = (next + 1) % kLoadBufs;
+            if (used[k]) VRT_CUDA(cudaEventSynchronize(done[k]));  // its previous upload + repack are done
+            used[k] = true;
+            uint8_t* hs = h_stage[k];
+            auto copy_rows = [&](uint32_t i0, uint32_t i1) {
+                for (uint32_t i = i0; i < i1; ++i) {
+                    memcpy(hs + i * take, src + (static_cast<uint64_t>(r0 + r + i)) * src_row_bytes + b0 * 34ull, take);
+                }
+            };
+            const unsigned T = static_cast<uint64_t>(n) * take >= (4ull << 20) ? workers : 1u;
+            if (T > 1) {
+                std::vector<std::thread> pool;
+                for (unsigned t = 1; t < T; ++t) pool.emplace_back(copy_rows, n * t / T, n * (t + 1) / T);
+                copy_rows(0, n / T);
+                for (auto& th : pool) th.join();
+            } else {
+                copy_rows(0, n);
             }
-            VRT_CUDA(cudaMemcpyAsync(d_stage, h_stage, n * take, cudaMemcpyHostToDevice, s));
-            RepackParams p{d_stage, take, 0, n, nb, dst, dst_cols, 0, mode};
+            VRT_CUDA(cudaMemcpyAsync(d_stage[k], hs, n * take, cudaMemcpyHostToDevice, s));
+            RepackParams p{d_stage[k], take, 0, n, nb, dst, dst_cols, 0, mode};
             if (mode == 0) {
                 p.dst_row0 = dst_row0 + r;
             } else {
@@ -620,7 +662,7 @@ struct Loader {
             }
             const uint64_t work = static_cast<uint64_t>(n) * nb;
             VRT_CUDA(launch(repack_kernel, dim3(static_cast<unsigned>((work + 255) / 256)), dim3(256), 0, s, false, p));
-            VRT_CUDA(cudaStreamSynchronize(s));
+            VRT_CUDA(cudaEventRecord(done[k], s));
         }
         return VRT_OK;
     }
@@ -682,12 +724,15 @@ static int load_weights(vrt_model* m, const vortexrt::GgufFile& g) {
         }
         return g.tensor_data(*t);
     };
+    // norm vectors: checked now, copied after the Q8_0 stream (a synchronous
+    // copy in between would drain the upload pipeline)
+    std::vector<std::pair<uint64_t, std::pair<const uint8_t*, uint64_t>>> norms;
     auto f32 = [&](const std::string& name, uint64_t n, uint64_t dst) -> int {
         const auto* t = g.find_tensor(name);
         if (!t || t->type != 0 || t->dimensions.size() != 1 || t->dimensions[0] != n) {
             return fail(VRT_E_INVALID, "Missing or mis-shaped Gemma 3 tensor: %s", name.c_str());
         }
-        VRT_CUDA(cudaMemcpy(m->arena + dst, g.tensor_data(*t), n * 4, cudaMemcpyHostToDevice));
+        norms.push_back({dst, {g.tensor_data(*t), n * 4}});
         return VRT_OK;
     };
     const uint8_t* emb = q8("token_embd.weight", d, c.vocab_size);
@@ -722,6 +767,10 @@ static int load_weights(vrt_model* m, const vortexrt::GgufFile& g) {
         VRT_TRY(f32(lname(l, "post_ffw_norm.weight"), d, L.n_post_ffw));
     }
     VRT_TRY(f32("output_norm.weight", d, m->out_norm));
+    VRT_TRY(ld.finish());
+    for (const auto& nv : norms) {
+        VRT_CUDA(cudaMemcpy(m->arena + nv.first, nv.second.first, nv.second.second, cudaMemcpyHostToDevice));
+    }
     return VRT_OK;
 }
 
