@@ -102,11 +102,26 @@ cudaError_t gemm_q8t_small(int epi, const TmaMap& hi, const TmaMap& lo, const Ge
 
 // K splits for a small-M GEMM: enough CTAs for two per SM, at least two
 // 128-column K tiles per split, at most 16 splits.
+// K ranges per (weight tile, token tile) of the small-M GEMM: one CTA per SM
+// is resident, so the cost of a split is modelled as waves x (K stages per
+// CTA + a fixed cost per CTA: ring fill and drain, the partial's write-out
+// and the last CTA's reduction), in 128-column stages.
 uint32_t gemm_small_ksplit(uint32_t n, uint32_t m, uint32_t k, int sms) {
+    constexpr double kFixedStages = 8.0;  // measured on 27B bs32: 2 -> +0%, 4 -> +3.5%, 8 -> +4.1% over 2 CTAs/SM
     const uint32_t tiles = (n / kGemmBN) * ((m + gemm_small_tile(m) - 1) / gemm_small_tile(m));
-    const uint32_t want = (2u * static_cast<uint32_t>(sms) + tiles - 1) / tiles;
-    const uint32_t kmax = std::max(1u, (k / kTileCols) / 2);
-    return std::max(1u, std::min({want, kmax, 16u}));
+    const uint32_t kt = k / kTileCols;
+    const uint32_t kmax = std::max(1u, std::min(kt / 2, 16u));
+    uint32_t best = 1;
+    double best_cost = 0.0;
+    for (uint32_t ks = 1; ks <= kmax; ++ks) {
+        const uint64_t waves = (static_cast<uint64_t>(tiles) * ks + sms - 1) / sms;
+        const double cost = static_cast<double>(waves) * (static_cast<double>(kt) / ks + kFixedStages);
+        if (ks == 1 || cost < best_cost) {
+            best = ks;
+            best_cost = cost;
+        }
+    }
+    return best;
 }
 
 uint32_t gemm_small_tile(uint32_t m) {
