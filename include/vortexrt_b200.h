@@ -182,6 +182,19 @@ VRT_API int vrt_q8t_gemm(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint
  * (src/q8_matvec.cpp:1360-2004 per token). */
 VRT_API int vrt_q8t_gemm_gelu(vrt_ctx* ctx, const void* d_packed_pair, uint32_t ffn, uint32_t cols,
                               const float* d_x, uint32_t m, float* d_act, void* stream);
+/* Few-row form on the integer tensor cores (tcgen05 kind::i8), 1 <= m <= 32:
+ * the packed matrix is first copied into the Q8M layout (128 x 128 int8
+ * operand tiles in the MMA's swizzled order + fp16 block scales; same byte
+ * count as the packed matrix), the activation rows are quantised per
+ * 32-block to int16 (split into two int8 halves), each Q8_0 block is one
+ * exact int32 MMA, and the block scales are applied in fp32 afterwards.
+ * Synchronous.  The gelu form takes a Q8M copy of a vrt_q8t_pack_pair matrix. */
+VRT_API int vrt_q8t_to_q8m(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint32_t cols, void* d_out,
+                           void* stream);
+VRT_API int vrt_q8m_gemm(vrt_ctx* ctx, const void* d_q8m, uint32_t rows, uint32_t cols, const float* d_x,
+                         uint32_t m, float* d_y, void* stream);
+VRT_API int vrt_q8m_gemm_gelu(vrt_ctx* ctx, const void* d_q8m_pair, uint32_t ffn, uint32_t cols,
+                              const float* d_x, uint32_t m, float* d_act, void* stream);
 /* LM head + argmax over a packed vocab matrix (logits written when d_logits != NULL). */
 VRT_API int vrt_q8t_lm_head_argmax(vrt_ctx* ctx, const void* d_packed, uint32_t vocab, uint32_t cols,
                                    const float* d_x, float* d_logits, vrt_argmax_result* d_out, void* stream);

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include "attention.cuh"
+#include "gemm_i8.cuh"
 #include "gemm_q8t.cuh"
 #include "gemv_q8t.cuh"
 
@@ -25,6 +26,14 @@ uint32_t gemm_small_tile(uint32_t m);
 uint32_t gemm_small_ksplit(uint32_t n, uint32_t m, uint32_t k, int sms);
 int make_f16_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 cudaError_t split_f16(const float* x, uint64_t n, __half* hi, __half* lo, cudaStream_t s);
+
+// Integer tensor-core GEMM for few activation rows (gemm_i8.cuh): Q8M copy
+// of a Q8T matrix, int16 split activations (operand maps over the int8
+// hi / lo arrays with 16-row boxes), p.nt = 16 or 32.
+cudaError_t q8t_to_q8m(const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t* dst, cudaStream_t s);
+cudaError_t quant_rows(const float* x, uint32_t ldx, uint32_t rows, uint32_t k, const Q16Out& o, cudaStream_t s);
+cudaError_t gemm_q8m_i8(int epi, const TmaMap& hi, const TmaMap& lo, const GemmI8Params& p, cudaStream_t s);
+int make_i8_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 
 // CTAs for a Q8T mat-vec: one per SM, at most one per row group.
 inline int gemv_grid(int sms, uint32_t rows) {

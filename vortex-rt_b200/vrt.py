@@ -111,6 +111,9 @@ _SIGS = {
     "vrt_batch_logits": (_i, [_vp, _u32, _vp]),
     "vrt_batch_last_ids": (_i, [_vp, _u32, _vp]),
     "vrt_q8t_gemm_gelu": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
+    "vrt_q8t_to_q8m": (_i, [_vp, _vp, _u32, _u32, _vp, _vp]),
+    "vrt_q8m_gemm": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
+    "vrt_q8m_gemm_gelu": (_i, [_vp, _vp, _u32, _u32, _vp, _u32, _vp, _vp]),
     "vrt_model_options_default": (None, [C.POINTER(ModelOptions)]),
     "vrt_model_load": (_i, [_vp, C.c_char_p, C.POINTER(ModelOptions), C.POINTER(_vp)]),
     "vrt_model_create_synthetic": (_i, [_vp, C.POINTER(Gemma3Config), _u64, C.POINTER(ModelOptions),
