@@ -100,6 +100,31 @@ def test_batch_270m_vs_single(ctx):
     b.close()
 
 
+def test_batch_fp16_forms_vs_single(ctx):
+    """Above 32 sequences the steps use the fp16 tensor-core forms (the
+    small-M kernel up to 64 rows, the 128-row kernel above): 80 sequences,
+    then the first 40, against single-sequence decoding."""
+    shape = sg.SHAPES["tiny-gqa"]
+    cfg = vrt.Gemma3Config.from_shape(shape)
+    model = vrt.Model(ctx, None, config=cfg, seed=77, max_positions=64)
+    single = vrt.Model(ctx, None, config=cfg, seed=77, max_positions=64, prefill_chunk=1)
+    rng = np.random.default_rng(9)
+    prompts = [[2] + rng.integers(3, shape.vocab_size, 3 + i % 7).tolist() for i in range(80)]
+    b = vrt.Batch(model, 80, 48)
+    for i, p in enumerate(prompts):
+        b.prefill(i, p)
+    b.decode_steps(80, 3)
+    b.decode_steps(40, 2)
+    for i in (0, 39, 40, 79):
+        ids, _ = b.read(i)
+        ref = single.generate(prompts[i], len(ids))
+        if ids != ref:  # allowed only from a near-tie of the single model on
+            k = next(j for j, (x, y) in enumerate(zip(ids, ref)) if x != y)
+            top2 = np.sort(_single_logits(single, prompts[i], ref[:k + 1]))[-2:]
+            assert top2[1] - top2[0] < 1e-3, (i, ids, ref)
+    b.close()
+
+
 def test_batch_27b_slice_vs_oracle(ctx):
     """27B widths (G = 2, hd 128, ffn 21504) on 6 layers, 3 sequences."""
     shape = sg.SHAPES["27b"].with_(block_count=6, vocab_size=16384, name="27b-slice")

@@ -73,8 +73,12 @@ __global__ void q8t_to_q8m_kernel(const uint8_t* __restrict__ src, uint32_t rows
         const uint32_t row = static_cast<uint32_t>(i / nb), blk = static_cast<uint32_t>(i % nb);
         uint8_t* tile = dst + q8m_tile(row / kQ8mRows, blk / 4, kts);
         const uint32_t r = row % kQ8mRows, c0 = (blk % 4) * 32;
-#pragma unroll 4
-        for (uint32_t e = 0; e < 32; ++e) tile[q8m_q_offset(r, c0 + e)] = src[q8t_weight_offset(row, blk * 32 + e, cols)];
+        // both layouts keep 16 consecutive columns of a row in one aligned 16-byte chunk
+#pragma unroll
+        for (uint32_t h = 0; h < 2; ++h) {
+            *reinterpret_cast<uint4*>(tile + q8m_q_offset(r, c0 + 16 * h)) =
+                *reinterpret_cast<const uint4*>(src + q8t_weight_offset(row, blk * 32 + 16 * h, cols));
+        }
         const uint64_t so = q8t_scale_offset(row, blk, cols);
         tile[q8m_s_offset(r, blk % 4)] = src[so];
         tile[q8m_s_offset(r, blk % 4) + 1] = src[so + 1];

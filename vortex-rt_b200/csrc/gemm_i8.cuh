@@ -95,7 +95,10 @@ struct GemmI8Params {
 constexpr int kI8Threads = 384;           // 12 warps
 constexpr int kI8WStages = 8;             // weight stages in shared memory (139 KB)
 constexpr int kI8XStages = 4;
-constexpr uint32_t kI8XStage = 2u * 32u * 128u;  // [hi rows | lo rows] x 128 bytes, NT <= 32
+// activation stage: [hi rows | lo rows] x 128 bytes (NT <= 32), then the
+// stage's block scales [4 blocks][32 rows] fp32; 1024-byte aligned stages
+constexpr uint32_t kI8XOps = 2u * 32u * 128u;
+constexpr uint32_t kI8XStage = kI8XOps + 1024u;
 constexpr uint32_t kI8Smem = 1024 + kI8WStages * kQ8mTileBytes + kI8XStages * kI8XStage +
                              8 * (2 * kI8WStages + 2 * kI8XStages + 4) + 16;
 
@@ -108,6 +111,30 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0u)
         : "memory");
+}
+
+// 16 consecutive 32-bit accumulator columns of this warp's 32 TMEM lanes,
+// no wait (the caller waits once for several loads).
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Exact int -> float for |v| < 2^22: the integer added to the bit pattern of
+// 1.5 * 2^23 lands in the mantissa, and subtracting 1.5 * 2^23 is exact
+// (FP32 add/sub pipes instead of the quarter-rate conversion unit).
+__device__ __forceinline__ float small_int_to_float(uint32_t v) {
+    return __fsub_rn(__int_as_float(static_cast<int>(v) + 0x4B400000), 12582912.0f);
 }
 
 template <int EPI>
@@ -145,7 +172,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
         }
         for (int d = 0; d < D; ++d) {
             mbar_init(&x_full[d], 1);
-            mbar_init(&x_empty[d], 1);
+            mbar_init(&x_empty[d], 1 + 8);  // MMA commit + the epilogue warps (block scales read)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
@@ -183,11 +210,16 @@ __global__ void __launch_bounds__(kI8Threads, 1)
                 const uint32_t d = kt % D;
                 if (kt >= static_cast<uint32_t>(D)) ok &= mbar_wait_bounded(&x_empty[d], ((kt / D) - 1) & 1);
                 uint8_t* st = xring + d * kI8XStage;
-                mbar_arrive_expect_tx(&x_full[d], 2 * NT * 128);
+                mbar_arrive_expect_tx(&x_full[d], 2 * NT * 128 + 4 * NT * 4);
                 const int kx = static_cast<int>((kt0 + kt) * kQ8mCols);  // int8: bytes = columns
                 for (uint32_t r0 = 0; r0 < NT; r0 += 16) {
                     tma_load_2d(st + r0 * 128, &x_hi, kx, static_cast<int>(t0 + r0), &x_full[d]);
                     tma_load_2d(st + (NT + r0) * 128, &x_lo, kx, static_cast<int>(t0 + r0), &x_full[d]);
+                }
+                // this stage's activation block scales (rows t0 .. t0 + NT of blocks 4 kt .. 4 kt + 3)
+                for (uint32_t b = 0; b < 4; ++b) {
+                    bulk_copy_g2s(st + kI8XOps + b * 128, p.sx + static_cast<uint64_t>((kt0 + kt) * 4 + b) * p.sx_ld + t0,
+                                  NT * 4, &x_full[d]);
                 }
             }
         }
@@ -219,7 +251,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
 #pragma unroll
         for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
         for (uint32_t kt = 0; kt < KT; ++kt) {
-            const uint32_t a = kt & 1, s = kt % S;
+            const uint32_t a = kt & 1, s = kt % S, d = kt % D;
             ok &= mbar_wait_bounded(&acc_full[a], (kt / 2) & 1);
             tc_fence_after();
             const uint2 sw = *reinterpret_cast<const uint2*>(wring + s * kQ8mTileBytes + q8m_s_offset(r, 0));
@@ -227,28 +259,43 @@ __global__ void __launch_bounds__(kI8Threads, 1)
             if (lane == 0) mbar_arrive(&w_empty[s]);
             const float wsc[4] = {half_bits_to_float(sw.x & 0xffffu), half_bits_to_float(sw.x >> 16),
                                   half_bits_to_float(sw.y & 0xffffu), half_bits_to_float(sw.y >> 16)};
-            const uint32_t kb0 = (kt0 + kt) * 4;
+            const float* sxs = reinterpret_cast<const float*>(xring + d * kI8XStage + kI8XOps);
+            // per block: 16 hi and 16 lo columns in two loads, one wait; the
+            // int32 block sums of each half are below 2^22 (32 * 127 * 128), so
+            // both convert exactly and 256 hi + lo is one rounding, the same
+            // as converting the combined int32
 #pragma unroll
             for (uint32_t b = 0; b < 4; ++b) {
-                const float* sxp = p.sx + static_cast<uint64_t>(kb0 + b) * p.sx_ld + t0 + cb;
                 const uint32_t col = a * 4 * BC + b * BC + cb;
+                uint32_t hv[16], lv[16];
+                if (hc == 16) {  // warp-uniform; never reads past this thread's columns of the block
+                    tmem_ld16_nowait(tmem + ((32 * q) << 16) + col, hv);
+                    tmem_ld16_nowait(tmem + ((32 * q) << 16) + col + NT, lv);
+                } else {
+                    tmem_ld8_nowait(tmem + ((32 * q) << 16) + col, hv);
+                    tmem_ld8_nowait(tmem + ((32 * q) << 16) + col + NT, lv);
 #pragma unroll
-                for (uint32_t j0 = 0; j0 < 16; j0 += 8) {
-                    if (j0 < hc) {  // warp-uniform
-                        uint32_t hv[8], lv[8];
-                        tmem_ld8(tmem + ((32 * q) << 16) + col + j0, hv);
-                        tmem_ld8(tmem + ((32 * q) << 16) + col + NT + j0, lv);
-                        const float4 x0 = *reinterpret_cast<const float4*>(sxp + j0);
-                        const float4 x1 = *reinterpret_cast<const float4*>(sxp + j0 + 4);
-                        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    for (int e = 8; e < 16; ++e) hv[e] = lv[e] = 0u;
+                }
+                float xs[16];
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            const int v = static_cast<int>(hv[e]) * 256 + static_cast<int>(lv[e]);
-                            sum[j0 + e] = __fadd_rn(sum[j0 + e], __fmul_rn(__fmul_rn(wsc[b], xs[e]), static_cast<float>(v)));
-                        }
-                    }
+                for (uint32_t j0 = 0; j0 < 16; j0 += 4) {
+                    const float4 x4 = j0 < hc ? *reinterpret_cast<const float4*>(sxs + b * 32 + cb + j0)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                    xs[j0] = x4.x;
+                    xs[j0 + 1] = x4.y;
+                    xs[j0 + 2] = x4.z;
+                    xs[j0 + 3] = x4.w;
+                }
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float v = __fmaf_rn(small_int_to_float(hv[e]), 256.0f, small_int_to_float(lv[e]));
+                    sum[e] = __fmaf_rn(__fmul_rn(wsc[b], xs[e]), v, sum[e]);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&x_empty[d]);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[a]);

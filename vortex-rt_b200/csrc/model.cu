@@ -308,6 +308,11 @@ struct vrt_model {
     float* tp_sum = nullptr;                            // reduced vectors, [2][d]
     uint32_t* tp_bar = nullptr;                         // grid barrier counter, generation
     float* logits_full = nullptr;                       // tensor parallel: all ranks' logits shards, [vocab]
+    // Q8M copies of the projections and the LM-head rows (integer tensor-core
+    // GEMM of batched decode), built at the first batch: per layer qkv, o, gu,
+    // down offsets, then the head
+    uint8_t* q8m = nullptr;
+    std::vector<uint64_t> q8m_off;
     // batched prefill buffers, [chunk][...] rows (allocated at the first batched prefill)
     struct Prefill {
         uint32_t cap = 0;
@@ -348,6 +353,14 @@ struct vrt_batch {
     std::vector<uint32_t> host_pos;            // positions as the host last set them
     cudaGraphExec_t graph = nullptr;
     uint32_t graph_count = 0;
+    // integer tensor-core GEMMs (count <= 32): int16 split operands [Sp][K]
+    // (row stride K of the GEMM at hand), block scales [K / 32][Sp], fp32
+    // attention output and gelu(gate) * up for their quantisation
+    bool i8 = false;
+    uint32_t Sp = 0;
+    int8_t *q_hi = nullptr, *q_lo = nullptr;
+    float *q_sx = nullptr, *att32 = nullptr, *act32 = nullptr;
+    vrt::TmaMap Qd_hi, Qd_lo, Qq_hi, Qq_lo, Qf_hi, Qf_lo;
 };
 
 namespace vrt {
@@ -1179,6 +1192,7 @@ static void destroy_model(vrt_model* m) {
     cudaFree(m->st);
     cudaFree(m->key_tmp);
     cudaFree(m->logits_full);
+    cudaFree(m->q8m);
     cudaFree(m->pf.mem);
     if (m->st_host) cudaFreeHost(m->st_host);
     if (m->hidden_host) cudaFreeHost(m->hidden_host);
@@ -1368,13 +1382,13 @@ static int prefill_layers(vrt_model* m, const SeqTarget& t, uint32_t n) {
         last = nc;
         embed_rows_kernel<<<nc, kRowThreads, 0, s>>>(m->arena + m->embd, t.prompt + p0, c.vocab_size, d,
                                                     std::sqrt(static_cast<float>(d)), F(m->layers[0].n_attn),
-                                                    c.rms_epsilon, B.h0, B.xh, B.xl, status);
+                                                    c.rms_epsilon, B.h0, B.xh, B.xl, Q16Out{}, status);
         VRT_CUDA(cudaGetLastError());
         for (uint32_t l = 0; l < c.block_count; ++l) {
             const auto& L = m->layers[l];
             if (l > 0) {
                 resid_rows_kernel<<<nc, kRowThreads, 0, s>>>(B.dn, B.h1, F(m->layers[l - 1].n_post_ffw), F(L.n_attn),
-                                                            c.rms_epsilon, d, B.h0, B.xh, B.xl, status);
+                                                            c.rms_epsilon, d, B.h0, B.xh, B.xl, Q16Out{}, status);
                 VRT_CUDA(cudaGetLastError());
             }
             VRT_TRY(gemm(kGemmStore, B.xd_hi, B.xd_lo, m->arena + L.qkv, m->qwl + 2 * m->kwl, d, nc, B.qkv, nullptr,
@@ -1401,7 +1415,7 @@ static int prefill_layers(vrt_model* m, const SeqTarget& t, uint32_t n) {
             VRT_TRY(gemm(kGemmStore, B.xq_hi, B.xq_lo, m->arena + L.o, d, m->qwl, nc, B.o, nullptr, nullptr));
             VRT_TRY(nccl_sum(m, B.o, static_cast<size_t>(nc) * d, s));  // row-parallel partials (tensor parallel)
             resid_rows_kernel<<<nc, kRowThreads, 0, s>>>(B.o, B.h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
-                                                        B.h1, B.xh, B.xl, status);
+                                                        B.h1, B.xh, B.xl, Q16Out{}, status);
             VRT_CUDA(cudaGetLastError());
             VRT_TRY(gemm(kGemmGeluSplit, B.xd_hi, B.xd_lo, m->arena + L.gu, 2 * m->ffl, d, nc, nullptr, B.ah, B.al));
             VRT_TRY(gemm(kGemmStore, B.xf_hi, B.xf_lo, m->arena + L.down, d, m->ffl, nc, B.dn, nullptr, nullptr));
@@ -1453,6 +1467,48 @@ static uint32_t batch_splits(const vrt_batch* b, uint32_t count, uint32_t cap) {
 }
 
 // Split-K workspace and tickets for the step's small-M GEMMs at `count` rows.
+// The Q8M copies of every projection and of this rank's LM-head rows, made
+// once per model from the Q8T arena (same byte count: 28.7 GB more for the
+// 27B shape).  Returns VRT_E_NOMEM, with nothing allocated, when they do not fit.
+static int model_q8m(vrt_model* m) {
+    if (m->q8m) return VRT_OK;
+    const auto& c = m->cfg;
+    const uint32_t d = c.embedding_length, kt = d / kTileCols, vl = m->vocab_hi - m->vocab_lo;
+    struct Mat { const uint8_t* src; uint32_t rows, cols; };
+    std::vector<Mat> mats;
+    for (const auto& L : m->layers) {
+        mats.push_back({m->arena + L.qkv, m->qwl + 2 * m->kwl, d});
+        mats.push_back({m->arena + L.o, d, m->qwl});
+        mats.push_back({m->arena + L.gu, 2 * m->ffl, d});
+        mats.push_back({m->arena + L.down, d, m->ffl});
+    }
+    mats.push_back({m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes, vl, d});
+    std::vector<uint64_t> off;
+    uint64_t total = 0;
+    for (const auto& x : mats) {
+        if (x.rows % kQ8mRows || x.cols % kQ8mCols) return fail(VRT_E_UNSUPPORTED, "Q8M needs 128-multiple shapes");
+        off.push_back(total);
+        total += align256(static_cast<uint64_t>(x.rows) * x.cols / 32 * 34);
+    }
+    uint8_t* mem = nullptr;
+    if (cudaMalloc(&mem, total) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(VRT_E_NOMEM, "no room for the Q8M weight copy (%.1f GB)", total / 1e9);
+    }
+    cudaStream_t s = m->ctx->stream;
+    for (size_t i = 0; i < mats.size(); ++i) {
+        const cudaError_t e = q8t_to_q8m(mats[i].src, mats[i].rows, mats[i].cols, mem + off[i], s);
+        if (e != cudaSuccess) {
+            cudaStreamSynchronize(s);
+            cudaFree(mem);
+            return cuda_fail(e, "q8t_to_q8m", __FILE__, __LINE__);
+        }
+    }
+    m->q8m = mem;
+    m->q8m_off = off;
+    return VRT_OK;
+}
+
 static int batch_gemm_workspace(vrt_batch* b, uint32_t count) {
     vrt_model* m = b->m;
     const auto& c = m->cfg;
@@ -1524,18 +1580,53 @@ static int batch_record_step(vrt_batch* b, uint32_t count) {
         VRT_CUDA(gemm_q8t_small(epi, hi, lo, p, s));
         return VRT_OK;
     };
+    // up to 32 sequences: integer tensor-core GEMMs on the Q8M copies, operands
+    // as int16 split halves (the row kernels and quant_rows write them)
+    const bool i8 = b->i8 && count <= 32;
+    auto q16 = [&](uint32_t K) { return i8 ? Q16Out{b->q_hi, b->q_lo, b->q_sx, K, b->Sp} : Q16Out{}; };
+    __half* oxh = i8 ? nullptr : b->xh;
+    __half* oxl = i8 ? nullptr : b->xl;
+    size_t wi = 0;  // next Q8M matrix: per layer qkv, o, gu, down, then the head
+    auto gemm8 = [&](int epi, const TmaMap& hi, const TmaMap& lo, uint32_t rows, uint32_t k, float* y,
+                     float* act) -> int {
+        GemmI8Params p{};
+        p.w = m->q8m + m->q8m_off[wi++];
+        p.n = rows;
+        p.k = k;
+        p.m = count;
+        p.sx = b->q_sx;
+        p.sx_ld = b->Sp;
+        p.y = y;
+        p.ldy = epi == kGemmArgmax ? c.vocab_size : rows;
+        p.act = act;
+        p.ld_act = rows / 2;
+        p.keys = b->keys;
+        p.row_base = epi == kGemmArgmax ? m->vocab_lo : 0u;
+        p.nt = gemm_small_tile(count);
+        p.ksplit = gemm_small_ksplit(rows, count, k, m->ctx->prop.multiProcessorCount);
+        p.ws = b->gws;
+        p.tickets = b->gtickets;
+        p.status = status;
+        VRT_CUDA(gemm_q8m_i8(epi, hi, lo, p, s));
+        return VRT_OK;
+    };
     embed_rows_kernel<<<count, kRowThreads, 0, s>>>(m->arena + m->embd, b->tokens, c.vocab_size, d,
                                                    std::sqrt(static_cast<float>(d)), F(m->layers[0].n_attn),
-                                                   c.rms_epsilon, b->h0, b->xh, b->xl, status);
+                                                   c.rms_epsilon, b->h0, oxh, oxl, q16(d), status);
     VRT_CUDA(cudaGetLastError());
     for (uint32_t l = 0; l < c.block_count; ++l) {
         const auto& L = m->layers[l];
         if (l > 0) {
             resid_rows_kernel<<<count, kRowThreads, 0, s>>>(b->dn, b->h1, F(m->layers[l - 1].n_post_ffw), F(L.n_attn),
-                                                           c.rms_epsilon, d, b->h0, b->xh, b->xl, status);
+                                                           c.rms_epsilon, d, b->h0, oxh, oxl, q16(d), status);
             VRT_CUDA(cudaGetLastError());
         }
-        VRT_TRY(gemm(kGemmStore, b->xd_hi, b->xd_lo, m->arena + L.qkv, qkvw, d, b->qkv, nullptr, nullptr));
+        wi = 4 * static_cast<size_t>(l);
+        if (i8) {
+            VRT_TRY(gemm8(kGemmStore, b->Qd_hi, b->Qd_lo, qkvw, d, b->qkv, nullptr));
+        } else {
+            VRT_TRY(gemm(kGemmStore, b->xd_hi, b->xd_lo, m->arena + L.qkv, qkvw, d, b->qkv, nullptr, nullptr));
+        }
         AttnParams a{};
         a.qkv = b->qkv;
         a.q_norm = F(L.n_q);
@@ -1559,28 +1650,48 @@ static int batch_record_step(vrt_batch* b, uint32_t count) {
         a.seq_qkv = qkvw;
         a.seq_cache = static_cast<uint64_t>(m->KVl) * b->cap[l] * hd;
         a.seq_out = m->qwl;
-        a.out_hi = b->xh;
-        a.out_lo = b->xl;
+        if (i8) {
+            a.out = b->att32;
+        } else {
+            a.out_hi = b->xh;
+            a.out_lo = b->xl;
+        }
         VRT_CUDA(attention_launch(a, dim3(a.splits, m->KVl, count), s, false));
-        VRT_TRY(gemm(kGemmStore, b->xq_hi, b->xq_lo, m->arena + L.o, d, m->qwl, b->o, nullptr, nullptr));
+        if (i8) {
+            VRT_CUDA(quant_rows(b->att32, m->qwl, count, m->qwl, q16(m->qwl), s));
+            VRT_TRY(gemm8(kGemmStore, b->Qq_hi, b->Qq_lo, d, m->qwl, b->o, nullptr));
+        } else {
+            VRT_TRY(gemm(kGemmStore, b->xq_hi, b->xq_lo, m->arena + L.o, d, m->qwl, b->o, nullptr, nullptr));
+        }
         VRT_TRY(nccl_sum(m, b->o, static_cast<size_t>(count) * d, s));  // row-parallel partials (tensor parallel)
         resid_rows_kernel<<<count, kRowThreads, 0, s>>>(b->o, b->h0, F(L.n_post_attn), F(L.n_ffn), c.rms_epsilon, d,
-                                                       b->h1, b->xh, b->xl, status);
+                                                       b->h1, oxh, oxl, q16(d), status);
         VRT_CUDA(cudaGetLastError());
-        VRT_TRY(gemm(kGemmGeluSplit, b->xd_hi, b->xd_lo, m->arena + L.gu, 2 * m->ffl, d, nullptr, b->ah, b->al));
-        VRT_TRY(gemm(kGemmStore, b->xf_hi, b->xf_lo, m->arena + L.down, d, m->ffl, b->dn, nullptr, nullptr));
+        if (i8) {
+            VRT_TRY(gemm8(kGemmGeluSplit, b->Qd_hi, b->Qd_lo, 2 * m->ffl, d, nullptr, b->act32));
+            VRT_CUDA(quant_rows(b->act32, m->ffl, count, m->ffl, q16(m->ffl), s));
+            VRT_TRY(gemm8(kGemmStore, b->Qf_hi, b->Qf_lo, d, m->ffl, b->dn, nullptr));
+        } else {
+            VRT_TRY(gemm(kGemmGeluSplit, b->xd_hi, b->xd_lo, m->arena + L.gu, 2 * m->ffl, d, nullptr, b->ah, b->al));
+            VRT_TRY(gemm(kGemmStore, b->xf_hi, b->xf_lo, m->arena + L.down, d, m->ffl, b->dn, nullptr, nullptr));
+        }
         VRT_TRY(nccl_sum(m, b->dn, static_cast<size_t>(count) * d, s));
     }
     const auto& lastL = m->layers[c.block_count - 1];
     final_rows_kernel<<<count, kRowThreads, 0, s>>>(b->dn, b->h1, F(lastL.n_post_ffw), F(m->out_norm), c.rms_epsilon, d,
-                                                   b->hidden, b->xh, b->xl, status);
+                                                   b->hidden, oxh, oxl, q16(d), status);
     VRT_CUDA(cudaGetLastError());
     // tied LM head over this rank's vocabulary rows; logits rows keep the
     // full-vocabulary stride (this rank's columns at vocab_lo)
     const uint32_t kt = d / kTileCols, vl = m->vocab_hi - m->vocab_lo;
-    VRT_TRY(gemm(kGemmArgmax, b->xd_hi, b->xd_lo,
-                 m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes, vl, d,
-                 b->keep_logits ? b->logits + m->vocab_lo : nullptr, nullptr, nullptr));
+    if (i8) {
+        wi = 4 * static_cast<size_t>(c.block_count);
+        VRT_TRY(gemm8(kGemmArgmax, b->Qd_hi, b->Qd_lo, vl, d, b->keep_logits ? b->logits + m->vocab_lo : nullptr, nullptr));
+    } else {
+        VRT_TRY(gemm(kGemmArgmax, b->xd_hi, b->xd_lo,
+                     m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes, vl, d,
+                     b->keep_logits ? b->logits + m->vocab_lo : nullptr, nullptr, nullptr));
+    }
     VRT_TRY(nccl_key_max(m, b->keys, count, s));
     batch_finalize_kernel<<<(count + 127) / 128, 128, 0, s>>>(b->keys, b->tokens, b->pos, b->out_ids, b->out_count,
                                                              b->out_cap, 0, count, c.vocab_size, 0, status);
@@ -2172,12 +2283,15 @@ int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, in
         sizes.push_back(S * m->KVl * cap * hd * 4);  // V
     }
     const uint64_t xw = std::max<uint64_t>(d, m->qwl);
+    const uint64_t Sp = (S + 31) / 32 * 32, kmax = std::max<uint64_t>(xw, m->ffl);
+    b->Sp = static_cast<uint32_t>(Sp);
     const uint64_t fixed[] = {S * 4, S * 4, S * b->out_cap * 4, S * 4, uint64_t(max_positions) * 4, S * 8,
                               S * m->KVl * 4,
                               S * d * 4, S * d * 4, S * (m->qwl + 2ull * m->kwl) * 4, S * d * 4, S * d * 4, S * d * 4,
                               b->keep_logits ? S * c.vocab_size * 4 : 0,
                               S * m->Hl * b->max_splits * 2 * 4, S * m->Hl * b->max_splits * hd * 4,
-                              S * xw * 2, S * xw * 2, S * m->ffl * 2, S * m->ffl * 2};
+                              S * xw * 2, S * xw * 2, S * m->ffl * 2, S * m->ffl * 2,
+                              Sp * kmax, Sp * kmax, kmax / 32 * Sp * 4, S * m->qwl * 4, S * m->ffl * 4};
     for (auto x : fixed) sizes.push_back(x);
     uint64_t total = 0;
     for (auto x : sizes) total += align256(x);
@@ -2206,6 +2320,11 @@ int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, in
     if (!b->keep_logits) b->logits = nullptr;
     __half** hl[] = {&b->xh, &b->xl, &b->ah, &b->al};
     for (auto h : hl) *h = reinterpret_cast<__half*>(take());
+    b->q_hi = reinterpret_cast<int8_t*>(take());
+    b->q_lo = reinterpret_cast<int8_t*>(take());
+    b->q_sx = reinterpret_cast<float*>(take());
+    b->att32 = reinterpret_cast<float*>(take());
+    b->act32 = reinterpret_cast<float*>(take());
     VRT_TRY(make_f16_tmap(&b->xd_hi, b->xh, S, d, 16));
     VRT_TRY(make_f16_tmap(&b->xd_lo, b->xl, S, d, 16));
     VRT_TRY(make_f16_tmap(&b->xq_hi, b->xh, S, m->qwl, 16));
@@ -2218,6 +2337,16 @@ int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, in
     VRT_TRY(make_f16_tmap(&b->Xq_lo, b->xl, S, m->qwl, 128));
     VRT_TRY(make_f16_tmap(&b->Xf_hi, b->ah, S, m->ffl, 128));
     VRT_TRY(make_f16_tmap(&b->Xf_lo, b->al, S, m->ffl, 128));
+    VRT_TRY(make_i8_tmap(&b->Qd_hi, b->q_hi, Sp, d, 16));
+    VRT_TRY(make_i8_tmap(&b->Qd_lo, b->q_lo, Sp, d, 16));
+    VRT_TRY(make_i8_tmap(&b->Qq_hi, b->q_hi, Sp, m->qwl, 16));
+    VRT_TRY(make_i8_tmap(&b->Qq_lo, b->q_lo, Sp, m->qwl, 16));
+    VRT_TRY(make_i8_tmap(&b->Qf_hi, b->q_hi, Sp, m->ffl, 16));
+    VRT_TRY(make_i8_tmap(&b->Qf_lo, b->q_lo, Sp, m->ffl, 16));
+    // steps of up to 32 sequences run the integer tensor-core GEMMs when the
+    // Q8M weight copy fits (else the fp16 form)
+    b->i8 = model_q8m(m) == VRT_OK;
+    if (!b->i8) clear_error();
     b->host_pos.assign(max_seqs, 0);
     VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
     *out = b.release();

@@ -13,7 +13,7 @@
 #include <cuda_fp16.h>
 
 #include "attention.cuh"
-#include "gemm_q8t.cuh"
+#include "gemm_i8.cuh"
 #include "vrt_device.cuh"
 
 namespace vrt {
@@ -39,12 +39,16 @@ __device__ __forceinline__ void store_split(__half* hi, __half* lo, uint64_t i, 
     lo[i] = l;
 }
 
+// The GEMM operand a row kernel writes: fp16 hi / lo terms (x_hi / x_lo,
+// when set) and/or the int16 split halves of the integer GEMM (q.hi, when
+// set; d % 32 == 0, so each warp holds whole 32-blocks).
 // Row m = token m of the chunk: h = token_embd[tok] * sqrt(d) -> h_out;
 // x = rms_norm_into(h, w_pre) -> x_hi / x_lo (the embedding prologue).
 __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const uint8_t* embd, const uint32_t* tokens,
                                                                  uint32_t vocab, uint32_t d, float emb_scale,
                                                                  const float* w_pre, float eps, float* h_out,
-                                                                 __half* x_hi, __half* x_lo, uint32_t* status) {
+                                                                 __half* x_hi, __half* x_lo, const Q16Out q,
+                                                                 uint32_t* status) {
     __shared__ double red[kRowThreads / 32];
     const uint32_t m = blockIdx.x;
     uint32_t tok = tokens[m];
@@ -72,7 +76,11 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const uint8_t* 
 #pragma unroll
     for (int u = 0; u < kRowMaxPerThread; ++u) {
         const uint32_t k = threadIdx.x + u * kRowThreads;
-        if (k < d) store_split(x_hi, x_lo, static_cast<uint64_t>(m) * d + k, __fmul_rn(__fmul_rn(h[u], scale), w_pre[k]));
+        if (k < d) {
+            const float v = __fmul_rn(__fmul_rn(h[u], scale), w_pre[k]);
+            if (x_hi) store_split(x_hi, x_lo, static_cast<uint64_t>(m) * d + k, v);
+            if (q.hi) warp_q16_store(q, m, k, v);
+        }
     }
 }
 
@@ -81,7 +89,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const uint8_t* 
 __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(const float* y, const float* h_prev,
                                                                  const float* w_post, const float* w_pre, float eps,
                                                                  uint32_t d, float* h_out, __half* x_hi, __half* x_lo,
-                                                                 uint32_t* status) {
+                                                                 const Q16Out q, uint32_t* status) {
     __shared__ double red[kRowThreads / 32];
     const uint64_t base = static_cast<uint64_t>(blockIdx.x) * d;
     float a[kRowMaxPerThread];
@@ -113,7 +121,11 @@ __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(const float* y,
 #pragma unroll
     for (int u = 0; u < kRowMaxPerThread; ++u) {
         const uint32_t k = threadIdx.x + u * kRowThreads;
-        if (k < d) store_split(x_hi, x_lo, base + k, __fmul_rn(__fmul_rn(a[u], sc), w_pre[k]));
+        if (k < d) {
+            const float v = __fmul_rn(__fmul_rn(a[u], sc), w_pre[k]);
+            if (x_hi) store_split(x_hi, x_lo, base + k, v);
+            if (q.hi) warp_q16_store(q, blockIdx.x, k, v);
+        }
     }
 }
 
@@ -123,7 +135,7 @@ __global__ void __launch_bounds__(kRowThreads) resid_rows_kernel(const float* y,
 __global__ void __launch_bounds__(kRowThreads) final_rows_kernel(const float* y, const float* h_prev,
                                                                  const float* w_post, const float* w_out, float eps,
                                                                  uint32_t d, float* hidden, __half* x_hi, __half* x_lo,
-                                                                 uint32_t* status) {
+                                                                 const Q16Out q, uint32_t* status) {
     __shared__ double red[kRowThreads / 32];
     const uint64_t base = static_cast<uint64_t>(blockIdx.x) * d;
     float a[kRowMaxPerThread];
@@ -157,7 +169,8 @@ __global__ void __launch_bounds__(kRowThreads) final_rows_kernel(const float* y,
         if (k < d) {
             const float v = __fmul_rn(a[u], __fmul_rn(sc, w_out[k]));
             hidden[base + k] = v;
-            store_split(x_hi, x_lo, base + k, v);
+            if (x_hi) store_split(x_hi, x_lo, base + k, v);
+            if (q.hi) warp_q16_store(q, blockIdx.x, k, v);
         }
     }
 }
