@@ -24,7 +24,7 @@
 // One CTA computes 128 weight rows x NT (16 or 32) activation rows over its
 // K range.  Warp roles: 0 weight stream (bulk copies, L2 prefetch ahead), 1
 // TMEM allocation + MMA issue (one thread), 2 activation stream (2-D TMA,
-// 128B swizzle), 4-11 epilogue (warp w reads TMEM lanes 32 (w % 4) ..; two
+// 128B swizzle), 4-19 epilogue (warp w reads TMEM lanes 32 (w % 4) ..; four
 // warps per lane quarter split the activation rows).  Two accumulator
 // buffers of four blocks each ping-pong between the MMA and the epilogue.
 // Every mbarrier wait is bounded; TMEM is always freed before exit.
@@ -92,7 +92,8 @@ struct GemmI8Params {
     uint32_t* status;
 };
 
-constexpr int kI8Threads = 384;           // 12 warps
+constexpr int kI8EpiWarps = 16;           // 4 TMEM lane quarters x 4 quarters of the activation rows
+constexpr int kI8Threads = (4 + kI8EpiWarps) * 32;
 constexpr int kI8WStages = 8;             // weight stages in shared memory (139 KB)
 constexpr int kI8XStages = 4;
 // activation stage: [hi rows | lo rows] x 128 bytes (NT <= 32), then the
@@ -126,6 +127,11 @@ __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[1
 __device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t* v) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld4_nowait(uint32_t taddr, uint32_t* v) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                  : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -168,15 +174,15 @@ __global__ void __launch_bounds__(kI8Threads, 1)
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&w_full[s], 1);
-            mbar_init(&w_empty[s], 1 + 8);  // MMA commit + the epilogue warps (block scales read)
+            mbar_init(&w_empty[s], 1 + kI8EpiWarps);  // MMA commit + the epilogue warps (block scales read)
         }
         for (int d = 0; d < D; ++d) {
             mbar_init(&x_full[d], 1);
-            mbar_init(&x_empty[d], 1 + 8);  // MMA commit + the epilogue warps (block scales read)
+            mbar_init(&x_empty[d], 1 + kI8EpiWarps);  // MMA commit + the epilogue warps (block scales read)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 8);
+            mbar_init(&acc_empty[a], kI8EpiWarps);
         }
         fence_mbar_init();
     }
@@ -244,12 +250,12 @@ __global__ void __launch_bounds__(kI8Threads, 1)
     } else if (warp >= 4) {
         // epilogue: lanes = weight rows n0 + 32 q + lane; activation rows [t0 + cb, t0 + cb + NT / 2)
         const uint32_t q = warp & 3;
-        const uint32_t hc = NT / 2;
+        const uint32_t hc = NT / 4;  // 8 or 4 activation rows per thread
         const uint32_t cb = ((warp - 4) >> 2) * hc;
         const uint32_t r = 32 * q + lane, row = n0 + r;
-        float sum[16];
+        float sum[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum[j] = 0.0f;
+        for (int j = 0; j < 8; ++j) sum[j] = 0.0f;
         for (uint32_t kt = 0; kt < KT; ++kt) {
             const uint32_t a = kt & 1, s = kt % S, d = kt % D;
             ok &= mbar_wait_bounded(&acc_full[a], (kt / 2) & 1);
@@ -260,26 +266,26 @@ __global__ void __launch_bounds__(kI8Threads, 1)
             const float wsc[4] = {half_bits_to_float(sw.x & 0xffffu), half_bits_to_float(sw.x >> 16),
                                   half_bits_to_float(sw.y & 0xffffu), half_bits_to_float(sw.y >> 16)};
             const float* sxs = reinterpret_cast<const float*>(xring + d * kI8XStage + kI8XOps);
-            // per block: 16 hi and 16 lo columns in two loads, one wait; the
+            // per block: this thread's hi and lo columns in two loads, one wait; the
             // int32 block sums of each half are below 2^22 (32 * 127 * 128), so
             // both convert exactly and 256 hi + lo is one rounding, the same
             // as converting the combined int32
 #pragma unroll
             for (uint32_t b = 0; b < 4; ++b) {
                 const uint32_t col = a * 4 * BC + b * BC + cb;
-                uint32_t hv[16], lv[16];
-                if (hc == 16) {  // warp-uniform; never reads past this thread's columns of the block
-                    tmem_ld16_nowait(tmem + ((32 * q) << 16) + col, hv);
-                    tmem_ld16_nowait(tmem + ((32 * q) << 16) + col + NT, lv);
-                } else {
+                uint32_t hv[8], lv[8];
+                if (hc == 8) {  // warp-uniform; never reads past this thread's columns of the block
                     tmem_ld8_nowait(tmem + ((32 * q) << 16) + col, hv);
                     tmem_ld8_nowait(tmem + ((32 * q) << 16) + col + NT, lv);
+                } else {
+                    tmem_ld4_nowait(tmem + ((32 * q) << 16) + col, hv);
+                    tmem_ld4_nowait(tmem + ((32 * q) << 16) + col + NT, lv);
 #pragma unroll
-                    for (int e = 8; e < 16; ++e) hv[e] = lv[e] = 0u;
+                    for (int e = 4; e < 8; ++e) hv[e] = lv[e] = 0u;
                 }
-                float xs[16];
+                float xs[8];
 #pragma unroll
-                for (uint32_t j0 = 0; j0 < 16; j0 += 4) {
+                for (uint32_t j0 = 0; j0 < 8; j0 += 4) {
                     const float4 x4 = j0 < hc ? *reinterpret_cast<const float4*>(sxs + b * 32 + cb + j0)
                                               : make_float4(0.f, 0.f, 0.f, 0.f);
                     xs[j0] = x4.x;
@@ -289,7 +295,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
                 }
                 tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
+                for (int e = 0; e < 8; ++e) {
                     const float v = __fmaf_rn(small_int_to_float(hv[e]), 256.0f, small_int_to_float(lv[e]));
                     sum[e] = __fmaf_rn(__fmul_rn(wsc[b], xs[e]), v, sum[e]);
                 }
@@ -306,21 +312,21 @@ __global__ void __launch_bounds__(kI8Threads, 1)
             const uint64_t mp = static_cast<uint64_t>(gridDim.y) * NT;
             float* mine = p.ws + static_cast<uint64_t>(blockIdx.z) * mp * p.n;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < 8; ++j) {
                 if (static_cast<uint32_t>(j) < hc) mine[(t0 + cb + j) * static_cast<uint64_t>(p.n) + row] = sum[j];
             }
             __threadfence();
-            named_bar_sync(2, 256);
+            named_bar_sync(2, kI8EpiWarps * 32);
             if (warp == 4 && lane == 0) {
                 const uint32_t tk = atomicAdd(p.tickets + blockIdx.y * gridDim.x + blockIdx.x, 1u);
                 last_cta = tk == p.ksplit - 1 ? 1u : 0u;
             }
-            named_bar_sync(2, 256);
+            named_bar_sync(2, kI8EpiWarps * 32);
             last = last_cta != 0;
             if (last) {
                 __threadfence();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
+                for (int j = 0; j < 8; ++j) {
                     if (static_cast<uint32_t>(j) < hc) {
                         float v = 0.0f;
                         for (uint32_t z = 0; z < p.ksplit; ++z) {
@@ -337,7 +343,7 @@ __global__ void __launch_bounds__(kI8Threads, 1)
         }
         if (last) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
+            for (int j = 0; j < 8; ++j) {
                 if (static_cast<uint32_t>(j) >= hc) continue;  // warp-uniform
                 const uint32_t tok = t0 + cb + j;
                 const float v = sum[j];
