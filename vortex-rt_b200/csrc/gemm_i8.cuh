@@ -136,13 +136,6 @@ __device__ __forceinline__ void tmem_ld4_nowait(uint32_t taddr, uint32_t* v) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Exact int -> float for |v| < 2^22: the integer added to the bit pattern of
-// 1.5 * 2^23 lands in the mantissa, and subtracting 1.5 * 2^23 is exact
-// (FP32 add/sub pipes instead of the quarter-rate conversion unit).
-__device__ __forceinline__ float small_int_to_float(uint32_t v) {
-    return __fsub_rn(__int_as_float(static_cast<int>(v) + 0x4B400000), 12582912.0f);
-}
-
 template <int EPI>
 __global__ void __launch_bounds__(kI8Threads, 1)
     q8m_gemm_i8_kernel(const __grid_constant__ TmaMap x_hi, const __grid_constant__ TmaMap x_lo, const GemmI8Params p) {
@@ -253,9 +246,9 @@ __global__ void __launch_bounds__(kI8Threads, 1)
         const uint32_t hc = NT / 4;  // 8 or 4 activation rows per thread
         const uint32_t cb = ((warp - 4) >> 2) * hc;
         const uint32_t r = 32 * q + lane, row = n0 + r;
-        float sum[8];
+        float2 acc[4];  // activation rows (2e, 2e + 1) of this thread, paired fp32 arithmetic
 #pragma unroll
-        for (int j = 0; j < 8; ++j) sum[j] = 0.0f;
+        for (int j = 0; j < 4; ++j) acc[j] = make_float2(0.0f, 0.0f);
         for (uint32_t kt = 0; kt < KT; ++kt) {
             const uint32_t a = kt & 1, s = kt % S, d = kt % D;
             ok &= mbar_wait_bounded(&acc_full[a], (kt / 2) & 1);
@@ -294,10 +287,23 @@ __global__ void __launch_bounds__(kI8Threads, 1)
                     xs[j0 + 3] = x4.w;
                 }
                 tmem_ld_wait();
+                // two activation rows per instruction (f32x2).  int -> float is
+                // exact for |v| < 2^22: the integer added to the bit pattern of
+                // 1.5 * 2^23 lands in the mantissa and subtracting 1.5 * 2^23 is
+                // exact (add pipe instead of the quarter-rate conversion unit);
+                // then 256 hi + lo, scale, accumulate -- each element rounded as alone
+                const float2 magic = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float v = __fmaf_rn(small_int_to_float(hv[e]), 256.0f, small_int_to_float(lv[e]));
-                    sum[e] = __fmaf_rn(__fmul_rn(wsc[b], xs[e]), v, sum[e]);
+                for (int e = 0; e < 8; e += 2) {
+                    const float2 h = __fadd2_rn(make_float2(__int_as_float(static_cast<int>(hv[e]) + 0x4B400000),
+                                                            __int_as_float(static_cast<int>(hv[e + 1]) + 0x4B400000)),
+                                                magic);
+                    const float2 l = __fadd2_rn(make_float2(__int_as_float(static_cast<int>(lv[e]) + 0x4B400000),
+                                                            __int_as_float(static_cast<int>(lv[e + 1]) + 0x4B400000)),
+                                                magic);
+                    const float2 v = __ffma2_rn(h, make_float2(256.0f, 256.0f), l);
+                    const float2 sc = __fmul2_rn(make_float2(wsc[b], wsc[b]), make_float2(xs[e], xs[e + 1]));
+                    acc[e / 2] = __ffma2_rn(sc, v, acc[e / 2]);
                 }
             }
             __syncwarp();
@@ -305,6 +311,12 @@ __global__ void __launch_bounds__(kI8Threads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+        float sum[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sum[2 * j] = acc[j].x;
+            sum[2 * j + 1] = acc[j].y;
         }
         bool last = true;
         if (p.ksplit > 1) {
