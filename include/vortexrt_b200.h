@@ -307,15 +307,20 @@ VRT_API int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, 
                                   float* ms_per_launch, uint64_t* algorithmic_bytes);
 
 /* ---------------------------------------------------------- batched decode
- * Independent sequences decoded together on one GPU (no reference
- * counterpart: the reference decodes one sequence, src/gemma3.cpp:1462-1882).
- * Each sequence has its own KV cache; a step decodes one greedy token for
- * each of the first `count` sequences, with the projections and the tied LM
- * head as tensor-core GEMMs of `count` rows.  Per sequence the results match
- * decoding it alone within the north-star tolerance. */
+ * Independent sequences decoded together (no reference counterpart: the
+ * reference decodes one sequence, src/gemma3.cpp:1462-1882), on one GPU or a
+ * tensor-parallel model (every rank holds every sequence; all ranks make the
+ * same calls).  Each sequence has its own KV cache; a step decodes one greedy
+ * token for each of the first `count` sequences, with the projections and the
+ * tied LM head as tensor-core GEMMs of `count` rows (integer tensor cores up to
+ * 32 rows, fp16 above).  Per sequence the results match decoding it alone
+ * within the north-star tolerance. */
 typedef struct vrt_batch vrt_batch;
 /* max_positions <= the model's positions; keep_logits != 0 keeps the last
- * step's full logits per sequence (max_seqs * vocab floats) for checking. */
+ * step's full logits per sequence (max_seqs * vocab floats) for checking.
+ * The first batch of a model also makes the model's Q8M weight copy for the
+ * integer GEMM (the size of the Q8_0 weights again; skipped, with the fp16
+ * GEMMs used instead, when it does not fit). */
 VRT_API int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, int keep_logits,
                              vrt_batch** out);
 VRT_API int vrt_batch_destroy(vrt_batch* b);
