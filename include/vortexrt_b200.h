@@ -188,7 +188,9 @@ VRT_API int vrt_q8t_gemm_gelu(vrt_ctx* ctx, const void* d_packed_pair, uint32_t 
  * count as the packed matrix), the activation rows are quantised per
  * 32-block to int16 (split into two int8 halves), each Q8_0 block is one
  * exact int32 MMA, and the block scales are applied in fp32 afterwards.
- * Synchronous.  The gelu form takes a Q8M copy of a vrt_q8t_pack_pair matrix. */
+ * Synchronous; uses the context scratch (about 2*m*cols bytes plus split-K
+ * partials), like vrt_q8t_gemm.  The gelu form takes a Q8M copy of a
+ * vrt_q8t_pack_pair matrix. */
 VRT_API int vrt_q8t_to_q8m(vrt_ctx* ctx, const void* d_packed, uint32_t rows, uint32_t cols, void* d_out,
                            void* stream);
 VRT_API int vrt_q8m_gemm(vrt_ctx* ctx, const void* d_q8m, uint32_t rows, uint32_t cols, const float* d_x,
