@@ -4,7 +4,8 @@ Default workload: the 27B-shaped decoder (vocab
 262144, d 5376, 62 layers, 32 q / 16 KV heads of 128, ffn 21504, window 1024,
 5:1 local:global) with seeded synthetic Q8_0 weights generated on the device,
 a 2048-token seeded prompt prefilled in one batched pass on the tensor cores
-(tcgen05 GEMMs; token by token under tensor parallelism), then greedy decode.
+(tcgen05 GEMMs; NCCL sums of the row-parallel partials under tensor
+parallelism), then greedy decode.
 `--workload 270m` runs config 0's 270M shape (8-token prompt) instead, and
 `--workload 270m-long` config 2 (270M, 4096-token prompt, decode past the
 512-token window).  Batched decode of independent sequences (tensor-core
@@ -388,7 +389,7 @@ def main():
         if dist_on:
             dist.barrier()
 
-    # prefill: one batched tensor-core pass on a single GPU, token by token under TP
+    # prefill: batched tensor-core passes (NCCL sums of the row-parallel partials under TP)
     stream = torch.cuda.ExternalStream(ctx.stream)
     pf0 = torch.cuda.Event(enable_timing=True)
     pf1 = torch.cuda.Event(enable_timing=True)
@@ -484,8 +485,8 @@ def main():
                          "ms_per_launch": k_ms, "traffic": tr},
             "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 40},
             "prefill": {"tokens": prompt_len, "s": t_pf, "tok_s": prompt_len / t_pf,
-                        "method": "token by token (tensor parallel)" if world > 1 else
-                                  "batched: tcgen05 Q8_0 GEMMs + tiled prefill attention, chunks of 2048"},
+                        "method": "batched: tcgen05 Q8_0 GEMMs + tiled prefill attention, chunks of 2048"
+                                  + (", NCCL sums of the row-parallel partials" if world > 1 else "")},
             "device_status": status,
             "clocks": clocks,
         }
