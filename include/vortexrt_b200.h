@@ -234,9 +234,10 @@ typedef struct {
 enum { VRT_TP_PEER = 0, VRT_TP_NCCL = 1 };
 
 /* Defaults: max_positions 0, single GPU, use_graph = 1, use_pdl = 1,
- * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0, prefill_chunk = 0.  Batched
- * prefill runs on one GPU (tp_world <= 1) without tracing; otherwise prompts
- * go token by token. */
+ * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0, prefill_chunk = 0.  Prompts of
+ * two or more tokens are prefilled in batched tensor-core passes (under
+ * tensor parallelism with NCCL sums of the row-parallel partials) unless
+ * tracing is on or prefill_chunk = 1; then they go token by token. */
 VRT_API void vrt_model_options_default(vrt_model_options* o);
 
 /* Load a Gemma 3 Q8_0 GGUF: weights repacked into the device arena, norms,
