@@ -221,7 +221,18 @@ typedef struct {
     uint32_t prefill_chunk; /* prompt tokens per batched (tensor-core) prefill
                                pass; 0 = 2048; 1 = token by token through the
                                decode step, the reference's method            */
+    int step_mode;          /* VRT_STEP_LAUNCHES (default) or VRT_STEP_PERSISTENT */
 } vrt_model_options;
+
+/* How one decode step runs on the GPU.  VRT_STEP_PERSISTENT: one cooperative
+ * kernel per token (one CTA per SM) streams every layer's weights without
+ * pausing at op boundaries and passes activations between CTAs as tagged
+ * words, with no grid barrier and no launch between ops.  VRT_STEP_LAUNCHES:
+ * one kernel per op (5 per layer), chained by programmatic dependent launch.
+ * The persistent form needs a single GPU or tp_exchange = VRT_TP_PEER; other
+ * cases use the launch chain.  Both give the same tokens up to fp32 addition
+ * order. */
+enum { VRT_STEP_PERSISTENT = 0, VRT_STEP_LAUNCHES = 1 };
 
 /* How the partial sums of the row-parallel projections (attention output,
  * FFN down) and the per-rank argmax keys are combined under tensor
@@ -234,7 +245,8 @@ typedef struct {
 enum { VRT_TP_PEER = 0, VRT_TP_NCCL = 1 };
 
 /* Defaults: max_positions 0, single GPU, use_graph = 1, use_pdl = 1,
- * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0, prefill_chunk = 0.  Prompts of
+ * tp_exchange = VRT_TP_PEER, tp_wait_ms = 0, prefill_chunk = 0,
+ * step_mode = VRT_STEP_LAUNCHES.  Prompts of
  * two or more tokens are prefilled in batched tensor-core passes (under
  * tensor parallelism with NCCL sums of the row-parallel partials) unless
  * tracing is on or prefill_chunk = 1; then they go token by token. */

@@ -38,6 +38,7 @@
 #include <vector>
 
 #include "prefill.cuh"
+#include "step_state.cuh"
 #include "vortexrt/gguf.hpp"
 #include "vrt_device.cuh"
 #include "vrt_internal.hpp"
@@ -147,21 +148,6 @@ __global__ void synth_norm_kernel(uint64_t key, uint32_t n, float mult, float* o
     if (i < n) out[i] = __fadd_rn(1.0f, __fmul_rn(static_cast<float>(irwin_hall4(key, i)), mult));
 }
 
-struct StepState {
-    uint32_t token;
-    uint32_t pos;
-    uint32_t status;
-    uint32_t out_count;
-    uint32_t prompt_count;
-    uint32_t result_index;
-    float result_value;
-    uint32_t pad;
-    unsigned long long key;
-    uint32_t epoch;  // steps run since creation; never reset (tensor-parallel exchange sequence numbers)
-    uint32_t pad2;
-};
-// Host writes (reset, prefill start) cover the fields before `epoch`.
-constexpr size_t kStepStateHostBytes = offsetof(StepState, epoch);
 
 __global__ void finalize_decode_kernel(StepState* st, uint32_t vocab, uint32_t* out_ids, uint32_t out_cap,
                                        const TpParams tp) {
@@ -308,6 +294,13 @@ struct vrt_model {
     float* tp_sum = nullptr;                            // reduced vectors, [2][d]
     uint32_t* tp_bar = nullptr;                         // grid barrier counter, generation
     float* logits_full = nullptr;                       // tensor parallel: all ranks' logits shards, [vocab]
+    // persistent decode step (one cooperative kernel per token)
+    bool ps_on = false;
+    vrt::PsParams ps{};             // launch parameters; head, trace set per launch
+    uint32_t ps_grid = 0, ps_smem = 0;
+    void* ps_mem = nullptr;         // layer table, exchange words, split scratch, tickets
+    unsigned long long** ps_rx_dev = nullptr;  // [world] receive-area bases
+    uint64_t ps_rx_offset = 0;      // words from the start of a rank's peer slots to its receive area
     // Q8M copies of the projections and the LM-head rows (integer tensor-core
     // GEMM of batched decode), built at the first batch: per layer qkv, o, gu,
     // down offsets, then the head
@@ -897,7 +890,193 @@ static std::vector<StepGemv> step_gemvs(vrt_model* m, bool head) {
     return v;
 }
 
+// ------------------------------------------------ persistent decode step
+
+// Most planes (CTAs holding a part of one row group) of a tile-granular span
+// of a rows x cols matrix over G CTAs.
+static uint32_t ps_max_planes(uint32_t rows, uint32_t cols, uint32_t G) {
+    const uint32_t kt = cols / kTileCols, groups = (rows + kTileRows - 1) / kTileRows, total = groups * kt;
+    uint32_t mx = 1;
+    for (uint32_t g = 0; g < groups; ++g) mx = std::max(mx, ps_planes_of(g, kt, total, G, nullptr));
+    return mx;
+}
+
+// Whether the step runs as one persistent kernel, and its sizes (grid, ring,
+// exchange planes, attention splits).  Host arithmetic plus kernel attribute
+// queries; runs before the tensor-parallel slots are allocated, since those
+// hold the kernel's receive areas.  Every CTA must own part of every
+// projection (the grid is capped by the smallest one): the order in which
+// exchange buffers are reused relies on each CTA publishing words in every op.
+static int ps_plan(vrt_model* m) {
+    m->ps_on = false;
+    if (m->opt.step_mode != VRT_STEP_PERSISTENT) return VRT_OK;
+    if (m->world > 1 && m->opt.tp_exchange != VRT_TP_PEER) return VRT_OK;
+    const auto& c = m->cfg;
+    const uint32_t d = c.embedding_length, hd = c.head_dim;
+    if (m->KVl == 0 || m->Hl % m->KVl != 0 || m->Hl / m->KVl > 8) return VRT_OK;
+    if (hd != 64 && hd != 128 && hd != 256) return VRT_OK;
+    auto tiles = [](uint64_t r, uint64_t k) { return (r + kTileRows - 1) / kTileRows * (k / kTileCols); };
+    const uint32_t qkv_rows = m->qwl + 2 * m->kwl;
+    uint64_t G = static_cast<uint64_t>(m->ctx->prop.multiProcessorCount);
+    G = std::min<uint64_t>(G, tiles(qkv_rows, d));
+    G = std::min<uint64_t>(G, tiles(d, m->qwl));
+    G = std::min<uint64_t>(G, (2ull * m->ffl + kTileRows - 1) / kTileRows);
+    G = std::min<uint64_t>(G, tiles(d, m->ffl));
+    if (G < 1) return VRT_OK;
+    // the device partition arithmetic is 32-bit: (tiles + 1) * G must fit
+    const uint64_t most = std::max({tiles(qkv_rows, d), tiles(d, m->qwl), tiles(2ull * m->ffl, d), tiles(d, m->ffl),
+                                    tiles(m->vocab_hi - m->vocab_lo, d)});
+    if ((most + 1) * G >= (1ull << 32)) return VRT_OK;
+    const uint32_t g32 = static_cast<uint32_t>(G);
+    PsParams p{};
+    p.L = c.block_count;
+    p.d = d;
+    p.H = m->Hl;
+    p.KV = m->KVl;
+    p.hd = hd;
+    p.qw = m->qwl;
+    p.kw = m->kwl;
+    p.ff = m->ffl;
+    p.vocab = c.vocab_size;
+    p.vl = m->vocab_hi - m->vocab_lo;
+    p.row_base = m->vocab_lo;
+    p.eps = c.rms_epsilon;
+    p.emb_scale = std::sqrt(static_cast<float>(d));
+    p.att_scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    p.rg = ps_rg_of(p.H, p.KV);
+    p.planes_qkv = ps_max_planes(qkv_rows, d, g32);
+    p.planes_rx = std::max(ps_max_planes(d, m->qwl, g32), ps_max_planes(d, m->ffl, g32));
+    if (p.planes_qkv > static_cast<uint32_t>(kPsMaxSlots) ||
+        p.planes_rx * static_cast<uint32_t>(m->world) > static_cast<uint32_t>(kPsMaxSlots)) {
+        return VRT_OK;
+    }
+    p.s_max = std::max(1u, std::min(64u, g32 / p.KV));
+    p.min_split = 64;
+    // tuning overrides (attention split size and count)
+    if (const char* e = getenv("VRT_PS_MIN_SPLIT")) p.min_split = std::max(1u, static_cast<uint32_t>(atoi(e)));
+    if (const char* e = getenv("VRT_PS_SPLITS")) p.s_max = std::max(1u, std::min(p.s_max, static_cast<uint32_t>(atoi(e))));
+    // LM-head rows prefetched into L2 while the last layers run: up to half of
+    // L2 over the grid, issued from the first layer after which the remaining
+    // layer weights fit in the other half.
+    const uint64_t l2 = static_cast<uint64_t>(m->ctx->prop.l2CacheSize);
+    const uint64_t layer_bytes = q8t_bytes(qkv_rows, d) + q8t_bytes(d, m->qwl) + q8t_bytes(2ull * m->ffl, d) +
+                                 q8t_bytes(d, m->ffl);
+    uint32_t pf_layer = p.L - 1;
+    while (pf_layer > 0 && layer_bytes * (p.L - pf_layer + 1) <= l2 / 2) --pf_layer;
+    p.head_pf_layer = pf_layer;
+    p.head_pf_bytes = static_cast<uint32_t>(std::min<uint64_t>(l2 / 2 / G, 1u << 30) & ~uint64_t(15));
+    const uint32_t wait_ms = m->opt.tp_wait_ms ? m->opt.tp_wait_ms : (m->world > 1 ? 10000u : 2000u);
+    p.wait_ns = static_cast<uint64_t>(wait_ms) * 1000000ull;
+    p.rank = static_cast<uint32_t>(m->rank);
+    p.world = static_cast<uint32_t>(m->world);
+    uint32_t max_dyn = 0;
+    int blocks = 0;
+    VRT_CUDA(ps_limits(hd, p.rg, 0, &max_dyn, nullptr));
+    p.ns = ps_ring_stages(p, max_dyn);
+    if (p.ns < 2) return VRT_OK;
+    const uint32_t smem = ps_smem_layout(p, p.ns).total;
+    VRT_CUDA(ps_limits(hd, p.rg, smem, &max_dyn, &blocks));
+    if (blocks < 1) return VRT_OK;
+    m->ps = p;
+    m->ps_smem = smem;
+    m->ps_grid = g32;
+    m->ps_on = true;
+    return VRT_OK;
+}
+
+// Device memory of the persistent step: layer table, exchange words (zero:
+// tag 0 never matches a sequence number), split scratch, tickets, and the
+// receive-area table (single GPU: a local area; tensor parallel: every rank's
+// area inside its mapped peer slots).
+static int ps_alloc(vrt_model* m) {
+    if (!m->ps_on) return VRT_OK;
+    PsParams& p = m->ps;
+    const auto& c = m->cfg;
+    const uint32_t L = p.L, d = p.d, W = p.world;
+    const uint64_t qkv_rows = p.qw + 2ull * p.kw;
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = align256(off + bytes);
+        return o;
+    };
+    const uint64_t o_layers = take(sizeof(PsLayer) * L);
+    const uint64_t o_qkv = take(8ull * 2 * p.planes_qkv * qkv_rows);
+    const uint64_t o_att = take(8ull * 2 * p.qw);
+    const uint64_t o_act = take(8ull * 2 * p.ff);
+    const uint64_t o_ml = take(4ull * p.H * p.s_max * 2);
+    const uint64_t o_acc = take(4ull * p.H * p.s_max * p.hd);
+    const uint64_t o_tk = take(4ull * (p.KV + 1));
+    const uint64_t o_rxt = take(8ull * W);
+    const uint64_t o_rx = W > 1 ? 0 : take(8ull * ps_rx_words(1, p.planes_rx, d));
+    VRT_CUDA(cudaMalloc(&m->ps_mem, off));
+    VRT_CUDA(cudaMemsetAsync(m->ps_mem, 0, off, m->ctx->stream));
+    uint8_t* base = static_cast<uint8_t*>(m->ps_mem);
+    auto F = [&](uint64_t o) { return reinterpret_cast<const float*>(m->arena + o); };
+    std::vector<PsLayer> ly(L);
+    for (uint32_t l = 0; l < L; ++l) {
+        const auto& S = m->layers[l];
+        PsLayer& t = ly[l];
+        t.qkv = m->arena + S.qkv;
+        t.o = m->arena + S.o;
+        t.gu = m->arena + S.gu;
+        t.down = m->arena + S.down;
+        t.n_attn = F(S.n_attn);
+        t.n_q = F(S.n_q);
+        t.n_k = F(S.n_k);
+        t.n_post_attn = F(S.n_post_attn);
+        t.n_ffn = F(S.n_ffn);
+        t.n_post_ffw = F(S.n_post_ffw);
+        t.k_cache = S.k_cache;
+        t.v_cache = S.v_cache;
+        t.rope_cos = S.global ? m->rope_cos_g : m->rope_cos_l;
+        t.rope_sin = S.global ? m->rope_sin_g : m->rope_sin_l;
+        t.cap = S.cap;
+        t.window = S.global ? 0u : c.sliding_window;
+    }
+    std::vector<unsigned long long*> rx(W);
+    for (uint32_t r = 0; r < W; ++r) {
+        rx[r] = W > 1 ? m->tp_peer_slots[r] + m->ps_rx_offset : reinterpret_cast<unsigned long long*>(base + o_rx);
+    }
+    VRT_CUDA(cudaMemcpyAsync(base + o_layers, ly.data(), sizeof(PsLayer) * L, cudaMemcpyHostToDevice, m->ctx->stream));
+    VRT_CUDA(cudaMemcpyAsync(base + o_rxt, rx.data(), 8ull * W, cudaMemcpyHostToDevice, m->ctx->stream));
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    p.layers = reinterpret_cast<const PsLayer*>(base + o_layers);
+    p.x_qkv = reinterpret_cast<unsigned long long*>(base + o_qkv);
+    p.x_att = reinterpret_cast<unsigned long long*>(base + o_att);
+    p.x_act = reinterpret_cast<unsigned long long*>(base + o_act);
+    p.part_ml = reinterpret_cast<float*>(base + o_ml);
+    p.part_acc = reinterpret_cast<float*>(base + o_acc);
+    p.att_tickets = reinterpret_cast<uint32_t*>(base + o_tk);
+    p.fin_ticket = p.att_tickets + p.KV;
+    p.rx = reinterpret_cast<unsigned long long* const*>(base + o_rxt);
+    const uint32_t kt = d / kTileCols;
+    p.embd = m->arena + m->embd;
+    p.lm = m->arena + m->embd + static_cast<uint64_t>(m->vocab_lo / kTileRows) * kt * kTileBytes;
+    p.out_norm = F(m->out_norm);
+    p.st = m->st;
+    p.out_ids = m->out_ids;
+    p.out_cap = kMaxSteps;
+    p.prompt = m->prompt;
+    p.hidden = m->hidden;
+    p.logits = m->logits;
+    p.trace = nullptr;
+#ifdef VRT_PS_STAMPS
+    VRT_CUDA(cudaMalloc(&p.stamps, 8ull * m->ps_grid * ps_stamp_count(L)));
+    VRT_CUDA(cudaMemset(p.stamps, 0, 8ull * m->ps_grid * ps_stamp_count(L)));
+#endif
+    return VRT_OK;
+}
+
 static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernels) {
+    if (m->ps_on) {
+        PsParams p = m->ps;
+        p.head = head ? 1u : 0u;
+        p.trace = m->trace_on ? m->trace : nullptr;
+        VRT_CUDA(ps_launch(p, m->ps_grid, m->ps_smem, s));
+        if (kernels) *kernels = 1;
+        return VRT_OK;
+    }
     const auto& c = m->cfg;
     const bool pdl = m->opt.use_pdl != 0;
     const int sms = m->ctx->prop.multiProcessorCount;
@@ -1098,7 +1277,9 @@ static int run_step(vrt_model* m, bool head) {
 static int tp_peer_setup(vrt_model* m) {
     const uint32_t d = m->cfg.embedding_length, W = static_cast<uint32_t>(m->world);
     cudaStream_t s = m->ctx->stream;
-    const uint64_t bytes = tp_slot_words(W, d) * 8;
+    // the persistent step's receive area follows the exchange slots
+    m->ps_rx_offset = tp_slot_words(W, d);
+    const uint64_t bytes = (tp_slot_words(W, d) + (m->ps_on ? ps_rx_words(W, m->ps.planes_rx, d) : 0)) * 8;
     VRT_CUDA(cudaMalloc(&m->tp_slots, bytes));
     VRT_CUDA(cudaMemsetAsync(m->tp_slots, 0, bytes, s));
     VRT_CUDA(cudaMalloc(&m->tp_sum, 2ull * d * 4 + 256));
@@ -1160,6 +1341,7 @@ static void tp_peer_teardown(vrt_model* m) {
 }
 
 static int finish_create(vrt_model* m) {
+    VRT_TRY(ps_plan(m));
     if (m->world > 1) {
         VRT_TRY(nccl_load(m->nccl));
         auto init = reinterpret_cast<CommInitRankFn>(dlsym(m->nccl.lib, "ncclCommInitRank"));
@@ -1170,6 +1352,7 @@ static int finish_create(vrt_model* m) {
         if (r) return fail(VRT_E_CUDA, "ncclCommInitRank failed: %s", m->nccl.GetErrorString(r));
         if (m->opt.tp_exchange == VRT_TP_PEER) VRT_TRY(tp_peer_setup(m));
     }
+    VRT_TRY(ps_alloc(m));
     VRT_TRY(build_graphs(m));
     return VRT_OK;
 }
@@ -1194,6 +1377,7 @@ static void destroy_model(vrt_model* m) {
     cudaFree(m->logits_full);
     cudaFree(m->q8m);
     cudaFree(m->pf.mem);
+    cudaFree(m->ps_mem);
     if (m->st_host) cudaFreeHost(m->st_host);
     if (m->hidden_host) cudaFreeHost(m->hidden_host);
     delete m;
@@ -1715,8 +1899,9 @@ static void batch_free(vrt_batch* b) {
 static int device_status(vrt_model* m, uint32_t& status) {
     status = m->st_host->status;
     if (!status) return VRT_OK;
-    const bool timeout = (status & (kStatusWaitTimeout | kStatusPeerTimeout)) != 0u;
+    const bool timeout = (status & (kStatusWaitTimeout | kStatusPeerTimeout | kStatusStepTimeout)) != 0u;
     const char* what = (status & kStatusPeerTimeout)   ? "a tensor-parallel peer did not answer in time"
+                       : (status & kStatusStepTimeout) ? "a persistent-step data wait timed out"
                        : (status & kStatusWaitTimeout) ? "a bounded device wait timed out"
                        : (status & kStatusBadToken)    ? "Token id is outside Gemma 3 vocabulary"
                                                        : "Non-finite value in the Gemma 3 hidden state or logits";
@@ -1734,6 +1919,7 @@ void vrt_model_options_default(vrt_model_options* o) {
     memset(o, 0, sizeof *o);
     o->use_graph = 1;
     o->use_pdl = 1;
+    o->step_mode = VRT_STEP_LAUNCHES;
 }
 
 int vrt_model_load(vrt_ctx* ctx, const char* path, const vrt_model_options* opts, vrt_model** out) {
@@ -1807,6 +1993,7 @@ int vrt_model_reset(vrt_model* m) {
     memset(m->st_host, 0, kStepStateHostBytes);
     VRT_CUDA(cudaMemcpyAsync(m->st, m->st_host, kStepStateHostBytes, cudaMemcpyHostToDevice, m->ctx->stream));
     if (m->tp_bar) VRT_CUDA(cudaMemsetAsync(m->tp_bar, 0, 8, m->ctx->stream));
+    if (m->ps_on) VRT_CUDA(cudaMemsetAsync(m->ps.att_tickets, 0, 4ull * (m->ps.KV + 1), m->ctx->stream));
     VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
     m->next_pos = 0;
     m->generated = 0;
@@ -2235,6 +2422,19 @@ int vrt_model_time_kernel(vrt_model* m, uint32_t layer, uint32_t which, uint32_t
     *ms_per_launch = ms / static_cast<float>(iters);
     return VRT_OK;
 }
+
+#ifdef VRT_PS_STAMPS
+// Timing builds only: the persistent step's phase stamps of the last step,
+// [grid][10 L + 10] globaltimer values; returns the count through *n.
+extern "C" VRT_API int vrt_ps_stamps(vrt_model* m, uint64_t* h_out, size_t cap, size_t* n) {
+    if (!m || !m->ps_on || !m->ps.stamps) return fail(VRT_E_STATE, "no stamps");
+    const size_t cnt = static_cast<size_t>(m->ps_grid) * ps_stamp_count(m->ps.L);
+    *n = cnt;
+    VRT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    VRT_CUDA(cudaMemcpy(h_out, m->ps.stamps, 8 * std::min(cap, cnt), cudaMemcpyDeviceToHost));
+    return VRT_OK;
+}
+#endif
 
 int vrt_tp_plan(const vrt_gemma3_config* cfg, int world, int rank, vrt_tp_shard* out) {
     clear_error();

@@ -7,6 +7,7 @@
 #include "gemm_i8.cuh"
 #include "gemm_q8t.cuh"
 #include "gemv_q8t.cuh"
+#include "step_persistent.cuh"
 
 namespace vrt {
 
@@ -34,6 +35,12 @@ cudaError_t q8t_to_q8m(const uint8_t* src, uint32_t rows, uint32_t cols, uint8_t
 cudaError_t quant_rows(const float* x, uint32_t ldx, uint32_t rows, uint32_t k, const Q16Out& o, cudaStream_t s);
 cudaError_t gemm_q8m_i8(int epi, const TmaMap& hi, const TmaMap& lo, const GemmI8Params& p, cudaStream_t s);
 int make_i8_tmap(TmaMap* out, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+
+// Persistent decode step (step.cu): raise the kernel's dynamic shared-memory
+// limit and report it (and, for `smem` bytes, the resident CTAs per SM);
+// cooperative launch of one step.
+cudaError_t ps_limits(uint32_t hd, uint32_t rg, uint32_t smem, uint32_t* max_dynamic, int* blocks_per_sm);
+cudaError_t ps_launch(const PsParams& p, uint32_t grid, uint32_t smem, cudaStream_t s);
 
 // CTAs for a Q8T mat-vec: one per SM, at most one per row group.
 inline int gemv_grid(int sms, uint32_t rows) {

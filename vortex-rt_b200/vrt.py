@@ -51,7 +51,8 @@ class Gemma3Config(C.Structure):
 class ModelOptions(C.Structure):
     _fields_ = [("max_positions", C.c_uint32), ("tp_rank", C.c_int), ("tp_world", C.c_int),
                 ("nccl_id", C.c_void_p), ("use_graph", C.c_int), ("use_pdl", C.c_int),
-                ("tp_exchange", C.c_int), ("tp_wait_ms", C.c_uint32), ("prefill_chunk", C.c_uint32)]
+                ("tp_exchange", C.c_int), ("tp_wait_ms", C.c_uint32), ("prefill_chunk", C.c_uint32),
+                ("step_mode", C.c_int)]
 
 
 class DeviceInfo(C.Structure):
@@ -234,7 +235,8 @@ class Model:
     def __init__(self, ctx: Context, path: str | None = None, *, config: Gemma3Config | None = None,
                  seed: int = 1234, max_positions: int = 0, use_graph: bool = True, use_pdl: bool = True,
                  tp_rank: int = 0, tp_world: int = 1, nccl_id: bytes | None = None,
-                 tp_exchange: str = "peer", tp_wait_ms: int = 0, prefill_chunk: int = 0):
+                 tp_exchange: str = "peer", tp_wait_ms: int = 0, prefill_chunk: int = 0,
+                 step_mode: str = "launches"):
         self.ctx = ctx
         self.h = _vp()
         self._batches = weakref.WeakSet()
@@ -248,6 +250,7 @@ class Model:
         o.tp_exchange = {"peer": 0, "nccl": 1}[tp_exchange]
         o.tp_wait_ms = tp_wait_ms
         o.prefill_chunk = prefill_chunk
+        o.step_mode = {"persistent": 0, "launches": 1}[step_mode]
         self._id = C.create_string_buffer(nccl_id, 128) if nccl_id else None
         o.nccl_id = C.cast(self._id, C.c_void_p) if self._id is not None else None
         self.h = _vp()
