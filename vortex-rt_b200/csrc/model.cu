@@ -965,6 +965,7 @@ static int ps_plan(vrt_model* m) {
     while (pf_layer > 0 && layer_bytes * (p.L - pf_layer + 1) <= l2 / 2) --pf_layer;
     p.head_pf_layer = pf_layer;
     p.head_pf_bytes = static_cast<uint32_t>(std::min<uint64_t>(l2 / 2 / G, 1u << 30) & ~uint64_t(15));
+    if (const char* e = getenv("VRT_PS_HEAD_PF")) p.head_pf_bytes = static_cast<uint32_t>(atoi(e)) & ~15u;  // tuning
     const uint32_t wait_ms = m->opt.tp_wait_ms ? m->opt.tp_wait_ms : (m->world > 1 ? 10000u : 2000u);
     p.wait_ns = static_cast<uint64_t>(wait_ms) * 1000000ull;
     p.rank = static_cast<uint32_t>(m->rank);

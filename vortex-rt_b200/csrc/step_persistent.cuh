@@ -68,6 +68,7 @@ constexpr int kPsMaxStages = 12;
 constexpr int kPsMaxSlots = 16;                 // ranks x planes added per element
 constexpr uint32_t kStatusStepTimeout = 1u << 4;
 constexpr uint32_t kPsWordsPerLayer = 5;        // qkv, attention, o, gelu*up, down
+constexpr int kPsVec4 = 6;                      // float4 per consumer thread in the norms: d <= 6144
 
 enum PsWord : uint32_t { kPsWQkv = 0, kPsWAtt = 1, kPsWO = 2, kPsWAct = 3, kPsWDn = 4 };
 
@@ -128,11 +129,20 @@ struct PsParams {
 // globaltimer at each phase boundary; 16 stamps per layer, then the head's.
 __host__ __device__ inline uint32_t ps_stamp_count(uint32_t L) { return 16 * L + 16; }
 #ifdef VRT_PS_STAMPS
+// cycles consumer thread 0 spends in ring waits [0] and data waits [1]
+__shared__ long long ps_dbg_cycles[2];
+#define VRT_PS_DBG_ADD(i, c) \
+    do {                     \
+        if (threadIdx.x == 0) ps_dbg_cycles[i] += (c); \
+    } while (0)
 #define VRT_PS_STAMP(k)                                                                       \
     do {                                                                                      \
         if (threadIdx.x == 0 && p.stamps) p.stamps[blockIdx.x * ps_stamp_count(p.L) + (k)] = global_ns(); \
     } while (0)
 #else
+#define VRT_PS_DBG_ADD(i, c) \
+    do {                     \
+    } while (0)
 #define VRT_PS_STAMP(k) \
     do {                \
     } while (0)
@@ -256,7 +266,14 @@ static __device__ __noinline__ bool ps_ring_wait_slow(uint64_t* bar, uint32_t pa
     return true;
 }
 __device__ __forceinline__ bool ps_ring_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+#ifdef VRT_PS_STAMPS
+    const long long c0 = clock64();
+    const bool r = mbar_try_wait(bar, parity) || ps_ring_wait_slow(bar, parity, status);
+    if (threadIdx.x < kPsConsumers) VRT_PS_DBG_ADD(0, clock64() - c0);
+    return r;
+#else
     return mbar_try_wait(bar, parity) || ps_ring_wait_slow(bar, parity, status);
+#endif
 }
 
 // Re-read *p until it carries `seq` or the wait expires; returns the word.
@@ -285,6 +302,32 @@ __device__ __forceinline__ unsigned long long ps_wait(const unsigned long long* 
 
 __device__ __forceinline__ float ps_val(unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); }
 
+// One thread of the CTA polls one word of the round until it is current
+// while the others wait at a barrier; then all threads load their words.
+// Polling by a single thread per CTA keeps the load traffic on the
+// producers' cache lines low (148 pollers instead of 38k), so their stores
+// land without queueing behind the polls.
+template <bool SYS>
+__device__ __forceinline__ void ps_cta_wait(const unsigned long long* w, uint32_t seq, uint64_t wait_ns,
+                                            uint32_t* status) {
+#ifdef VRT_PS_STAMPS
+    const long long c0 = clock64();
+#endif
+    if (threadIdx.x == 0) {
+        const unsigned long long x = ps_ld_s<SYS>(w);
+        if (static_cast<uint32_t>(x >> 32) != seq) ps_wait_slow<SYS>(w, x, seq, wait_ns, status);
+    }
+    named_bar_sync(1, kPsConsumers);
+#ifdef VRT_PS_STAMPS
+    VRT_PS_DBG_ADD(1, clock64() - c0);
+#endif
+}
+
+__device__ __forceinline__ double ps_sq4(const float4& v) {
+    return static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y + static_cast<double>(v.z) * v.z +
+           static_cast<double>(v.w) * v.w;
+}
+
 // Sum of the 256 consumer threads' doubles in a fixed order, broadcast.
 __device__ __forceinline__ double ps_sum(double v, double* red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -310,7 +353,9 @@ __device__ void ps_gather_t(const unsigned long long* base, uint32_t src_stride,
                             uint32_t world, uint32_t rows_op, uint32_t kt, uint32_t G, uint32_t n, RowOf row_of,
                             uint32_t seq, float* dst, uint64_t wait_ns, uint32_t* status) {
     const uint32_t total = (rows_op + kTileRows - 1) / kTileRows * kt;
-    for (uint32_t i0 = threadIdx.x; i0 < n; i0 += EB * kPsConsumers) {
+    for (uint32_t r0 = 0; r0 < n; r0 += EB * kPsConsumers) {  // same rounds in every thread (barrier below)
+        if (r0 == 0) ps_cta_wait<SYS>(base + row_of(0), seq, wait_ns, status);
+        const uint32_t i0 = r0 + threadIdx.x;
         unsigned long long w[EB][MAXQ];
         const unsigned long long* a[EB][MAXQ];
         uint32_t nq[EB];
@@ -396,6 +441,7 @@ __device__ inline void ps_poll_quant(const unsigned long long* base, uint32_t n,
     constexpr int U = 6, GROUPS = kPsConsumers / 8;
     const uint32_t nblk = n / 32;
     for (uint32_t r0 = 0; r0 < nblk; r0 += U * GROUPS) {  // same trip count in every lane (shuffles below)
+        if (r0 == 0) ps_cta_wait<false>(base, seq, wait_ns, status);
         const uint32_t b0 = r0 + (tid >> 3);
         unsigned long long w[U][4];
 #pragma unroll
@@ -448,9 +494,28 @@ __device__ inline void ps_poll_quant(const unsigned long long* base, uint32_t n,
     }
 }
 
-// Quantise xs[0, K) (fp32 in shared memory) into x16p / sx, one block per thread.
+// Quantise xs[0, K) (fp32 in shared memory) into x16p / sx exactly as
+// quant_block does: eight threads per 32-block, four elements each.
 __device__ __forceinline__ void ps_quant_smem(const float* xs, uint32_t K, int16_t* x16p, float* sx) {
-    for (uint32_t blk = threadIdx.x; blk < K / 32; blk += kPsConsumers) quant_block(xs + blk * 32, blk, x16p, sx);
+    const int tid = threadIdx.x, sub = tid & 7;
+    const uint32_t nblk = K / 32;
+    for (uint32_t r0 = 0; r0 < nblk; r0 += kPsConsumers / 8) {  // same trip count in every lane (shuffles)
+        const uint32_t blk = r0 + (tid >> 3);
+        const bool ok = blk < nblk;
+        const float4 x = ok ? reinterpret_cast<const float4*>(xs)[blk * 8 + sub] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float amax = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        if (!ok) continue;
+        const float sc = quant_scale(amax);
+        const float inv = amax > 0.0f ? 32767.0f / amax : 0.0f;
+        if (sub == 0) sx[blk] = sc;
+        const int q0 = quant_one(x.x, inv), q1 = quant_one(x.y, inv), q2 = quant_one(x.z, inv), q3 = quant_one(x.w, inv);
+        *reinterpret_cast<uint2*>(x16p + x16p_index(blk * 32 + sub * 4)) =
+            make_uint2((static_cast<uint32_t>(q0) & 0xffffu) | (static_cast<uint32_t>(q1) << 16),
+                       (static_cast<uint32_t>(q2) & 0xffffu) | (static_cast<uint32_t>(q3) << 16));
+    }
 }
 
 // ------------------------------------------------------------ the ring
@@ -641,12 +706,34 @@ __device__ __forceinline__ void ps_load_kv(float (&kb)[P][M], float (&vb)[P][M],
     }
 }
 
+// Per-head RMSNorm (fp64 sum of squares) + NeoX RoPE of one head held in a
+// warp (lane l: dims l + 32 m), weights and rope row already in registers;
+// the arithmetic of head_norm_rope (src/gemma3.cpp:1045-1104, 1371-1424).
+template <int M>
+__device__ __forceinline__ void ps_norm_rope(float (&v)[M], const float (&w)[M], const float (&rc)[M / 2],
+                                             const float (&rs)[M / 2], uint32_t hd, float eps) {
+    double ss = 0.0;
+#pragma unroll
+    for (int m = 0; m < M; ++m) ss += static_cast<double>(v[m]) * static_cast<double>(v[m]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float scale = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(hd)) + eps);
+#pragma unroll
+    for (int m = 0; m < M; ++m) v[m] = __fmul_rn(v[m], __fmul_rn(scale, w[m]));
+#pragma unroll
+    for (int m = 0; m < M / 2; ++m) {
+        const float a = v[m], b = v[m + M / 2];
+        v[m] = __fsub_rn(__fmul_rn(a, rc[m]), __fmul_rn(b, rs[m]));
+        v[m + M / 2] = __fadd_rn(__fmul_rn(b, rc[m]), __fmul_rn(a, rs[m]));
+    }
+}
+
 // One attention item: KV head g, history split s of `used`, positions
-// [t0, t1).  qkv_s holds the gathered q rows of the R heads, then k, then v
-// (fp32); the result goes to the attention-output words (seq).
-template <int M, int RG>
+// [t0, t1).  gather() fills qkv_s with the q rows of the group's R heads,
+// then k, then v (fp32); the result goes to the attention-output words (seq).
+template <int M, int RG, typename Gather>
 __device__ void ps_attention_item(const PsParams& p, const PsLayer& Ly, uint32_t g, uint32_t s, uint32_t used,
-                                  uint32_t t0, uint32_t t1, uint32_t pos, float* qkv_s,
+                                  uint32_t t0, uint32_t t1, uint32_t pos, float* qkv_s, Gather gather,
                                   float* att_smem, unsigned long long* att_words, uint32_t seq, uint32_t* status) {
     constexpr int HD = M * 32;
     constexpr int P = M >= 8 ? 2 : 4;  // positions per warp step (eight warps; register budget of 168)
@@ -665,15 +752,30 @@ __device__ void ps_attention_item(const PsParams& p, const PsLayer& Ly, uint32_t
     const float* vc = Ly.v_cache + static_cast<uint64_t>(g) * Ly.cap * hd;
     const bool has_new = t0 < t1 && t1 == pos + 1;
 
-    // first batch of cached positions in flight during the query prologue
+    // Everything that does not depend on this step's projections goes out
+    // before the wait for q / k / v: the first batch of cached positions, the
+    // RoPE row of this position and both head-norm weights.
     float kb[P][M], vb[P][M];
     ps_load_kv<M, P>(kb, vb, kc, vc, t0 + warp, t1, pos, Ly.cap, hd, lane);
+    float wq[M], wk[M], rc[M / 2], rs[M / 2];
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        wq[m] = __ldg(Ly.n_q + lane + 32 * m);
+        wk[m] = __ldg(Ly.n_k + lane + 32 * m);
+    }
+#pragma unroll
+    for (int m = 0; m < M / 2; ++m) {
+        rc[m] = __ldg(cs + lane + 32 * m);
+        rs[m] = __ldg(sn + lane + 32 * m);
+    }
+    gather();  // q rows of the group's heads, then k, then v -> qkv_s
+    named_bar_sync(1, kPsConsumers);
 
     for (uint32_t r = warp; r <= R; r += kPsWarps) {
         float v[M];
 #pragma unroll
         for (int m = 0; m < M; ++m) v[m] = qkv_s[r * hd + lane + 32 * m];
-        head_norm_rope<M>(v, r < R ? Ly.n_q : Ly.n_k, cs, sn, hd, p.eps, lane);
+        ps_norm_rope<M>(v, r < R ? wq : wk, rc, rs, hd, p.eps);
         if (r < R) {
 #pragma unroll
             for (int m = 0; m < M; ++m) q_s[r * HD + lane + 32 * m] = v[m];
@@ -932,6 +1034,10 @@ __global__ void __launch_bounds__(kPsThreads, 1) ps_step_kernel(const PsParams p
 
     // ---------------------------------------------------------- consumers
     VRT_PS_STAMP(16 * L + 2);
+#ifdef VRT_PS_STAMPS
+    const long long ps_c_start = clock64();
+    if (tid == 0) ps_dbg_cycles[0] = ps_dbg_cycles[1] = 0;
+#endif
     for (int i = tid; i < 2 * kPsWarps * 8 * 16; i += kPsConsumers) partial[i] = 0.0f;
     const uint32_t epoch = p.st->epoch;
     const uint32_t pos = p.st->pos;
@@ -945,26 +1051,92 @@ __global__ void __launch_bounds__(kPsThreads, 1) ps_step_kernel(const PsParams p
     // residual update from gathered partials (already in v): h = v * (s * w_post) + h,
     // then x = rms_norm_into(h, w_pre) (or the final rms_norm_inplace) into v
     auto residual = [&](const float* w_post, const float* w_pre, float* trace_row, bool final_norm) {
-        double so = 0.0;
-        for (uint32_t k = tid; k < d; k += kPsConsumers) so += static_cast<double>(v[k]) * v[k];
-        so = ps_sum(so, red);
-        const float ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(d)) + p.eps);
-        double ss = 0.0;
-        bool bad = false;
-        for (uint32_t k = tid; k < d; k += kPsConsumers) {
-            const float hk = __fadd_rn(__fmul_rn(v[k], __fmul_rn(ps, w_post[k])), h[k]);
-            h[k] = hk;
-            bad |= !isfinite(hk);
-            if (b == 0 && trace_row) trace_row[k] = hk;
-            ss += static_cast<double>(hk) * hk;
-        }
-        if (bad && b == 0) atomicOr(status, kStatusNonFinite);
-        ss = ps_sum(ss, red);
-        const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(d)) + p.eps);
-        for (uint32_t k = tid; k < d; k += kPsConsumers) {
-            const float x = final_norm ? __fmul_rn(h[k], __fmul_rn(sc, w_pre[k])) : __fmul_rn(__fmul_rn(h[k], sc), w_pre[k]);
-            v[k] = x;
-            if (final_norm && b == 0) p.hidden[k] = x;
+        if (d <= 4u * kPsVec4 * kPsConsumers) {
+            // every load of the thread (smem vectors, both norm weights) in flight at once
+            const uint32_t n4 = d / 4;
+            float4* v4 = reinterpret_cast<float4*>(v);
+            float4* h4 = reinterpret_cast<float4*>(h);
+            const float4* wp4 = reinterpret_cast<const float4*>(w_post);
+            const float4* wq4 = reinterpret_cast<const float4*>(w_pre);
+            float4 a[kPsVec4], hh[kPsVec4], wp[kPsVec4], wq[kPsVec4];
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < kPsVec4; ++u) {
+                const uint32_t i = tid + u * kPsConsumers;
+                const bool ok = i < n4;
+                wp[u] = ok ? __ldg(wp4 + i) : z;
+                wq[u] = ok ? __ldg(wq4 + i) : z;
+                a[u] = ok ? v4[i] : z;
+                hh[u] = ok ? h4[i] : z;
+            }
+            double so = 0.0;
+#pragma unroll
+            for (int u = 0; u < kPsVec4; ++u) so += ps_sq4(a[u]);
+            so = ps_sum(so, red);
+            const float ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(d)) + p.eps);
+            double ss = 0.0;
+            bool bad = false;
+#pragma unroll
+            for (int u = 0; u < kPsVec4; ++u) {
+                const uint32_t i = tid + u * kPsConsumers;
+                float4 x;
+                x.x = __fadd_rn(__fmul_rn(a[u].x, __fmul_rn(ps, wp[u].x)), hh[u].x);
+                x.y = __fadd_rn(__fmul_rn(a[u].y, __fmul_rn(ps, wp[u].y)), hh[u].y);
+                x.z = __fadd_rn(__fmul_rn(a[u].z, __fmul_rn(ps, wp[u].z)), hh[u].z);
+                x.w = __fadd_rn(__fmul_rn(a[u].w, __fmul_rn(ps, wp[u].w)), hh[u].w);
+                hh[u] = x;
+                if (i < n4) {
+                    h4[i] = x;
+                    bad |= !(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w));
+                    if (b == 0 && trace_row) reinterpret_cast<float4*>(trace_row)[i] = x;
+                }
+                ss += ps_sq4(x);
+            }
+            if (bad && b == 0) atomicOr(status, kStatusNonFinite);
+            ss = ps_sum(ss, red);
+            const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(d)) + p.eps);
+#pragma unroll
+            for (int u = 0; u < kPsVec4; ++u) {
+                const uint32_t i = tid + u * kPsConsumers;
+                if (i >= n4) continue;
+                float4 x;
+                if (final_norm) {  // rms_norm_inplace: h * (scale * w)
+                    x.x = __fmul_rn(hh[u].x, __fmul_rn(sc, wq[u].x));
+                    x.y = __fmul_rn(hh[u].y, __fmul_rn(sc, wq[u].y));
+                    x.z = __fmul_rn(hh[u].z, __fmul_rn(sc, wq[u].z));
+                    x.w = __fmul_rn(hh[u].w, __fmul_rn(sc, wq[u].w));
+                    if (b == 0) reinterpret_cast<float4*>(p.hidden)[i] = x;
+                } else {           // rms_norm_into: (h * scale) * w
+                    x.x = __fmul_rn(__fmul_rn(hh[u].x, sc), wq[u].x);
+                    x.y = __fmul_rn(__fmul_rn(hh[u].y, sc), wq[u].y);
+                    x.z = __fmul_rn(__fmul_rn(hh[u].z, sc), wq[u].z);
+                    x.w = __fmul_rn(__fmul_rn(hh[u].w, sc), wq[u].w);
+                }
+                v4[i] = x;
+            }
+        } else {
+            // wider than any Gemma 3 model: looped form
+            double so = 0.0;
+            for (uint32_t k = tid; k < d; k += kPsConsumers) so += static_cast<double>(v[k]) * v[k];
+            so = ps_sum(so, red);
+            const float ps = 1.0f / sqrtf(static_cast<float>(so / static_cast<double>(d)) + p.eps);
+            double ss = 0.0;
+            bool bad = false;
+            for (uint32_t k = tid; k < d; k += kPsConsumers) {
+                const float hk = __fadd_rn(__fmul_rn(v[k], __fmul_rn(ps, w_post[k])), h[k]);
+                h[k] = hk;
+                bad |= !isfinite(hk);
+                if (b == 0 && trace_row) trace_row[k] = hk;
+                ss += static_cast<double>(hk) * hk;
+            }
+            if (bad && b == 0) atomicOr(status, kStatusNonFinite);
+            ss = ps_sum(ss, red);
+            const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(d)) + p.eps);
+            for (uint32_t k = tid; k < d; k += kPsConsumers) {
+                const float x = final_norm ? __fmul_rn(h[k], __fmul_rn(sc, w_pre[k])) : __fmul_rn(__fmul_rn(h[k], sc), w_pre[k]);
+                v[k] = x;
+                if (final_norm && b == 0) p.hidden[k] = x;
+            }
         }
         named_bar_sync(1, kPsConsumers);
     };
@@ -992,17 +1164,40 @@ __global__ void __launch_bounds__(kPsThreads, 1) ps_step_kernel(const PsParams p
                 token = 0;
             }
             double ss = 0.0;
-            for (uint32_t k = tid; k < d; k += kPsConsumers) {
-                const int8_t q = static_cast<int8_t>(p.embd[q8t_weight_offset(token, k, d)]);
-                const uint64_t so = q8t_scale_offset(token, k / 32, d);
-                const float sc = half_bits_to_float(p.embd[so] | (static_cast<uint32_t>(p.embd[so + 1]) << 8));
-                const float hk = __fmul_rn(__fmul_rn(sc, static_cast<float>(q)), p.emb_scale);
-                h[k] = hk;
-                ss += static_cast<double>(hk) * hk;
+            for (uint32_t k0 = 0; k0 < d; k0 += 8 * kPsConsumers) {  // eight elements per thread in flight
+                int8_t q[8];
+                uint32_t sb[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint32_t k = k0 + tid + u * kPsConsumers;
+                    const uint64_t so = q8t_scale_offset(token, k / 32, d);
+                    q[u] = k < d ? static_cast<int8_t>(p.embd[q8t_weight_offset(token, k, d)]) : int8_t(0);
+                    sb[u] = k < d ? (p.embd[so] | (static_cast<uint32_t>(p.embd[so + 1]) << 8)) : 0u;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint32_t k = k0 + tid + u * kPsConsumers;
+                    if (k >= d) continue;
+                    const float hk = __fmul_rn(__fmul_rn(half_bits_to_float(sb[u]), static_cast<float>(q[u])), p.emb_scale);
+                    h[k] = hk;
+                    ss += static_cast<double>(hk) * hk;
+                }
             }
             ss = ps_sum(ss, red);
             const float sc = 1.0f / sqrtf(static_cast<float>(ss / static_cast<double>(d)) + p.eps);
-            for (uint32_t k = tid; k < d; k += kPsConsumers) v[k] = __fmul_rn(__fmul_rn(h[k], sc), Ly.n_attn[k]);
+            for (uint32_t k0 = 0; k0 < d; k0 += 8 * kPsConsumers) {
+                float w[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint32_t k = k0 + tid + u * kPsConsumers;
+                    w[u] = k < d ? __ldg(Ly.n_attn + k) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint32_t k = k0 + tid + u * kPsConsumers;
+                    if (k < d) v[k] = __fmul_rn(__fmul_rn(h[k], sc), w[u]);
+                }
+            }
             named_bar_sync(1, kPsConsumers);
         } else {
             gather_rx(1, par ^ 1u, p.ff, SEQ(l - 1, kPsWDn));
@@ -1045,11 +1240,12 @@ __global__ void __launch_bounds__(kPsThreads, 1) ps_step_kernel(const PsParams p
                     const uint32_t qn = R_heads * hd;
                     return i < qn ? g * qn + i : (i < qn + hd ? qw + g * hd + (i - qn) : qw + kw + g * hd + (i - qn - hd));
                 };
-                ps_gather<false>(p.x_qkv + par * p.planes_qkv * qkv_plane, 0, qkv_plane, 1, qkv_rows, d / kTileCols, G,
-                                 (R_heads + 2) * hd, row_of, SEQ(l, kPsWQkv), v, p.wait_ns, status, p.planes_qkv);
-                named_bar_sync(1, kPsConsumers);
-                VRT_PS_STAMP(16 * l + 3);
-                ps_attention_item<M, RG>(p, Ly, g, s, used, t0, t1, pos, v, att_smem, p.x_att + par * p.qw,
+                auto gather = [&]() {
+                    ps_gather<false>(p.x_qkv + par * p.planes_qkv * qkv_plane, 0, qkv_plane, 1, qkv_rows, d / kTileCols,
+                                     G, (R_heads + 2) * hd, row_of, SEQ(l, kPsWQkv), v, p.wait_ns, status, p.planes_qkv);
+                    VRT_PS_STAMP(16 * l + 3);
+                };
+                ps_attention_item<M, RG>(p, Ly, g, s, used, t0, t1, pos, v, gather, att_smem, p.x_att + par * p.qw,
                                          SEQ(l, kPsWAtt), status);
                 named_bar_sync(1, kPsConsumers);
             }
@@ -1128,6 +1324,14 @@ __global__ void __launch_bounds__(kPsThreads, 1) ps_step_kernel(const PsParams p
         if (tid == 0 && best) atomicMax(&p.st->key, best);
     }
     VRT_PS_STAMP(16 * L + 1);
+#ifdef VRT_PS_STAMPS
+    if (tid == 0 && p.stamps) {
+        unsigned long long* st_ = p.stamps + blockIdx.x * ps_stamp_count(p.L) + 16 * L;
+        st_[4] = ps_dbg_cycles[0];
+        st_[5] = ps_dbg_cycles[1];
+        st_[6] = clock64() - ps_c_start;
+    }
+#endif
 
     // ---- finalize: the last CTA to get here
     __shared__ uint32_t ps_fin_last;
