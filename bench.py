@@ -1,48 +1,57 @@
-"""Benchmark of the Gemma 3 Q8_0 token loop on B200 (bs=1 greedy decode).
+"""Benchmark of the Gemma 3 Q8_0 token loop on B200.
 
 Default workload: the 27B-shaped decoder (vocab
 262144, d 5376, 62 layers, 32 q / 16 KV heads of 128, ffn 21504, window 1024,
 5:1 local:global) with seeded synthetic Q8_0 weights generated on the device,
 a 2048-token seeded prompt prefilled in one batched pass on the tensor cores
 (tcgen05 GEMMs; NCCL sums of the row-parallel partials under tensor
-parallelism), then greedy decode.
-`--workload 270m` runs config 0's 270M shape (8-token prompt) instead, and
-`--workload 270m-long` config 2 (270M, 4096-token prompt, decode past the
-512-token window).  Batched decode of independent sequences (tensor-core
-GEMMs with M = sequences, per-sequence KV caches): `--workload 270m-batch`
-is config 3 (256 sequences x 1024-token prompts, split evenly over the N
-ranks as replicas with no collective), `--workload 27b-bs32` config 4 at
-batch 32 on one GPU.
+parallelism), then greedy decode at batch 1.  Under torchrun (N > 1) the
+model is tensor-parallel over N GPUs (Q/K/V, gate, up column-sharded; o-proj,
+down row-sharded, their partial sums exchanged over NVLink peer memory inside
+the consuming kernel; vocab-sharded LM head), so the N ranks decode the same
+tokens: value = tokens / max-over-ranks time ("scaling": "strong").
 
-One step = one decoded token (batch 1).  Under torchrun (N > 1) the model is
-tensor-parallel over N GPUs (Q/K/V, gate, up column-sharded; o-proj, down
-row-sharded with an NCCL all-reduce; vocab-sharded LM head with an NCCL max
-of the argmax keys), so the N ranks decode the same tokens: value = tokens /
-max-over-ranks time ("scaling": "strong").
+Other workloads: `270m` (config 0), `270m-long` (config 2: 4096-token
+prefill, decode past the 512 window), `270m-batch` (config 3: 256 sequences x
+1024-token prompts, split over the ranks as replicas), `27b-bs32` (config 4 at
+batch 32), `sweep` (config 1: the isolated Q8_0 mat-vec / FFN / LM-head
+shapes, 1000 iterations each, hot and cold HBM).
 
-Printed JSON line:
-  value          decode tok/s, K steps device-resident (graph replays, token fed
-                 back on the device), CUDA events on the model stream
+Printed JSON line (rank 0):
+  value          decode tok/s over K device-resident steps (graph replays,
+                 token fed back on the device), CUDA events on the model stream
   e2e            tok/s through vrt_decode_step (the C ABI call a caller makes):
-                 host token + position copied in, argmax result copied out, per step
-  roofline       the dominant kernel (layer gate/up mat-vec: RMSNorm prologue,
-                 gelu*up epilogue) timed alone on the same stream; algorithmic
-                 bytes / time vs the measured HBM peak
-  cpu_baseline   the CPU oracle (C restatement of the reference token loop,
-                 GQA-generalised; the reference itself refuses head_count_kv != 1)
-                 on a bounded sample, extrapolated to one token
-  prefill        the prompt's prefill, device-timed (CUDA events), tokens/s
-  clocks         nvidia-smi samples taken during the timed region
+                 token + position copied in, argmax result copied out, per step
+  roofline       the dominant kernel (layer gate/up mat-vec) timed alone on the
+                 same stream: algorithmic bytes / time vs the measured HBM peak
+  step_roofline  whole step: weights + norms + KV bytes per token / step time
+  ids            the greedy ids decoded in the timed region (first 8, count,
+                 SHA-1) and the smallest top-2 logit margin over them (a
+                 teacher-forced replay of the same steps with top-2 logits), so
+                 lines at different N can be checked for the same stream
+  cpu_baseline   the CPU oracle timed on whole decode tokens of the same model
+                 shape on this box's host cores (config 0: the reference's own
+                 token loop, oracle/_ref)
+  prefill        the prompt's prefill, device-timed, tokens/s
+  clocks         SM clock / throttle reasons sampled in-process (NVML, 10 ms)
+                 during the timed region
+  also           (default workload, one GPU) config 0 and the config 1 sweep,
+                 measured in the same run
+`--impl reference` runs the reference arm: the reference's CPU token loop
+(oracle/_ref for the 270M shape; the C restatement of it where the reference
+refuses the shape, e.g. 16 KV heads) on whole tokens of the same workload.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -56,6 +65,7 @@ import synth_gguf as sg  # noqa: E402
 PROMPT_LEN = {"27b": 2048, "270m": 8, "270m-long": 4096, "270m-batch": 1024, "27b-bs32": 2048}
 BATCH_SEQS = {"270m-batch": 256, "27b-bs32": 32}
 METRIC = "decode tok/s (Gemma3-shaped Q8_0, bs=1 greedy)"
+SEED = 1234
 
 
 def measured_peaks():
@@ -75,51 +85,122 @@ def committed_traffic(workload: str):
     return None
 
 
+# ------------------------------------------------------------------ clocks
+
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """SM clock, power and throttle reasons of this rank's GPU, sampled every
+    10 ms in-process through NVML (read-only queries); nvidia-smi at 200 ms
+    when NVML is not importable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
-        self.rows: list[list[str]] = []
-        self.proc = None
+    def __init__(self, local: int):
+        self.local = local
+        self.rows = []
+        self.stop_ev = threading.Event()
+        self.thread = None
+        self.source = None
+        self.h = None
+        self.nv = None
+
+    def _handle(self):
+        import pynvml as nv
+        import torch
+        nv.nvmlInit()
+        props = torch.cuda.get_device_properties(self.local)
+        tries = [f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0",
+                 f"{props.pci_domain_id:04X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"]
+        for t in tries:
+            try:
+                return nv, nv.nvmlDeviceGetHandleByPciBusId(t)
+            except Exception:  # noqa: BLE001 - try the next form
+                pass
+        return nv, nv.nvmlDeviceGetHandleByIndex(self.local)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            threading.Thread(target=self._read, daemon=True).start()
+            self.nv, self.h = self._handle()
+            self.source = "nvml, 10 ms"
+            self.max_mhz = float(self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            get_reasons = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                                  getattr(self.nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+
+            def loop():
+                while not self.stop_ev.is_set():
+                    try:
+                        self.rows.append((float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)),
+                                          int(get_reasons(self.h)) if get_reasons else 0,
+                                          self.nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0))
+                    except Exception:  # noqa: BLE001 - a failed sample is skipped
+                        pass
+                    self.stop_ev.wait(0.010)
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.source = "nvidia-smi, 200 ms"
+            self._smi_start()
+
+    def _smi_start(self):
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.local), "--query-gpu=" + fields,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+        def rd():
+            for line in self.proc.stdout:
+                r = [x.strip() for x in line.split(",")]
+                if len(r) < 7:
+                    continue
+                try:
+                    bits = sum(self.REASONS[n] for n, v in zip(names, r[3:7]) if v.lower() == "active")
+                    self.max_mhz = float(r[1])
+                    self.rows.append((float(r[0]), bits, float(r[2])))
+                except ValueError:
+                    pass
 
-    def stop(self):
-        if self.proc:
+        self.thread = threading.Thread(target=rd, daemon=True)
+        self.thread.start()
+
+    def stop(self) -> dict:
+        self.stop_ev.set()
+        if getattr(self, "proc", None):
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-        rows = [r for r in self.rows if len(r) >= 9]
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.thread:
+            self.thread.join(timeout=2)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "source": self.source}
+        sm = [r[0] for r in self.rows]
+        bits = 0
+        for r in self.rows:
+            bits |= r[1]
+        reasons = sorted(n for n, b in self.REASONS.items() if bits & b)
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": getattr(self, "max_mhz", None),
+                "power_w_max": max(r[2] for r in self.rows), "reasons": reasons, "samples": len(self.rows),
+                "source": self.source}
 
 
-def shape_for(workload: str) -> sg.Gemma3Shape:
-    return sg.SHAPES["27b" if workload.startswith("27b") else "270m"]
+# ------------------------------------------------------------------ shapes
+
+def shape_for(workload: str, layers: int = 0, vocab: int = 0) -> sg.Gemma3Shape:
+    s = sg.SHAPES["27b" if workload.startswith("27b") else "270m"]
+    if layers:
+        s = s.with_(block_count=layers)
+    if vocab:
+        s = s.with_(vocab_size=vocab)
+    return s
 
 
 def bytes_per_token(shape: sg.Gemma3Shape, pos: int) -> int:
@@ -137,62 +218,528 @@ def bytes_per_token(shape: sg.Gemma3Shape, pos: int) -> int:
     return w + norms + d // 32 * 34 + kv
 
 
-def cpu_baseline(workload: str, threads: int) -> dict:
-    """Oracle port timed on a bounded sample of one decode token."""
+def prompt_ids(shape: sg.Gemma3Shape, n: int, seed: int = 4) -> list[int]:
+    return [2] + np.random.default_rng(seed).integers(3, shape.vocab_size, n - 1).tolist()
+
+
+def workload_config(workload: str, shape: sg.Gemma3Shape, world: int, prompt_len: int, warmup: int, steps: int,
+                    tp_exchange: str) -> dict:
+    """The `config` object of the JSON line: identical for both arms."""
+    name = {"27b": f"config 4: 27B-shaped Gemma 3 Q8_0, bs=1 greedy decode after a {prompt_len}-token prefill",
+            "270m": f"config 0: 270M-shaped Gemma 3 Q8_0, bs=1 greedy decode after {prompt_len} prompt tokens",
+            "270m-long": f"config 2: 270M-shaped Gemma 3 Q8_0, {prompt_len}-token batched prefill, then bs=1 "
+                         "greedy decode past the 512-token window"}[workload]
+    step_bytes = bytes_per_token(shape, prompt_len + warmup + steps // 2)
+    return {"workload": name, "d_model": shape.embedding_length, "layers": shape.block_count,
+            "heads": f"{shape.head_count}q/{shape.head_count_kv}kv x {shape.head_dim}",
+            "ffn": shape.feed_forward_length, "vocab": shape.vocab_size, "global_batch": 1,
+            "positions": f"{prompt_len + warmup}..{prompt_len + warmup + steps}",
+            "parallelism": f"tp{world}" if world > 1 else "single GPU",
+            "tp_exchange": (("peer memory (partials pushed over NVLink, summed in the consumer kernel)"
+                             if tp_exchange == "peer" else "NCCL all-reduce") if world > 1 else None),
+            "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB streamed per token)"}
+
+
+# ------------------------------------------------------------ CPU baselines
+
+def cpu_tokens(shape: sg.Gemma3Shape, threads: int, warm: int, n: int, prompt: list[int]) -> dict:
+    """Whole decode tokens of the C restatement of the reference token loop
+    (GQA-generalised) on a host copy of the same seeded model."""
     import oracle as O
 
-    shape = shape_for(workload)
-    if not workload.startswith("27b"):
-        sample_layers, sample_vocab = shape.block_count, shape.vocab_size
-    else:
-        sample_layers, sample_vocab = 2, 16384
-    small = shape.with_(block_count=sample_layers, vocab_size=sample_vocab)
-    o = O.Oracle(shape=small, seed=11, threads=threads, max_positions=8)
-    o.decode(2, 0, 1)  # warm caches / page in
-    o.reset()
     t0 = time.perf_counter()
-    steps = 2
-    for p in range(steps):
-        o.decode(2 + p, p, 1)
-    t_tok = (time.perf_counter() - t0) / steps
-    # LM head slice alone, to split head vs layer time
-    raw = O.synth_q8(11, "token_embd.weight", sample_vocab, shape.embedding_length)
-    x = np.random.default_rng(0).standard_normal(shape.embedding_length).astype(np.float32)
-    t1 = time.perf_counter()
-    O.q8_matvec(raw, x, sample_vocab, lanes=64 if shape.embedding_length > 1024 else 8, threads=threads)
-    t_head = time.perf_counter() - t1
-    per_layer = max(t_tok - t_head, 1e-9) / sample_layers
-    full = per_layer * shape.block_count + t_head * (shape.vocab_size / sample_vocab)
+    o = O.Oracle(shape=shape, seed=SEED, threads=threads, max_positions=warm + n + 2)
+    create_s = time.perf_counter() - t0
+    toks = prompt + [prompt[-1]] * (warm + n)
+    for p in range(warm):
+        o.decode(toks[p], p, 1)
+    times = []
+    for p in range(warm, warm + n):
+        t = time.perf_counter()
+        o.decode(toks[p], p, 1)
+        times.append(time.perf_counter() - t)
     o.close()
-    return {"value": 1.0 / full, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} decode tokens of a {sample_layers}-layer, {sample_vocab}-row-vocab slice of the "
-                      f"{workload} shape + one LM-head slice mat-vec, extrapolated to {shape.block_count} layers and "
-                      f"vocab {shape.vocab_size}; C restatement of src/gemma3.cpp (the reference itself refuses "
-                      f"head_count_kv != 1), {threads} host threads"}
+    return {"tok_s": n / sum(times), "per_token_s": times, "create_s": create_s}
+
+
+def cpu_reference_270m(threads: int, prompt: list[int], n: int, warm: int = 0) -> dict | None:
+    """The reference's own token loop (src/gemma3.cpp via oracle/_ref) on the
+    270M synthetic GGUF: greedy tokens after the prompt, timed per token."""
+    import oracle as O
+
+    if not O.reference_available():
+        return None
+    shape = sg.SHAPES["270m"]
+    d = os.path.join(tempfile.gettempdir(), "vrt_bench_models")
+    path = sg.cached_model(shape, SEED, d)
+    r = O.Reference(path, threads=threads)
+    for p, t in enumerate(prompt[:-1]):
+        r.decode(t, p, 0)
+    tok, pos = prompt[-1], len(prompt) - 1
+    times = []
+    for i in range(warm + n):
+        t = time.perf_counter()
+        _, ids, _ = r.decode(tok, pos, 1)
+        if i >= warm:
+            times.append(time.perf_counter() - t)
+        tok, pos = int(ids[0]), pos + 1
+    r.close()
+    return {"tok_s": len(times) / sum(times), "per_token_s": times}
+
+
+def cpu_baseline(workload: str, shape: sg.Gemma3Shape, threads: int) -> dict:
+    prompt = prompt_ids(shape, 8)
+    if workload.startswith("270m"):
+        r = cpu_reference_270m(threads, prompt, 8, warm=1)
+        if r is not None:
+            return {"value": r["tok_s"], "unit": "tok/s", "cores": threads, "kind": "reference",
+                    "sample": f"8 whole greedy decode tokens (after 1 warm-up) following an 8-token prompt, the "
+                              f"reference's own src/gemma3.cpp token loop (oracle/_ref) on the same seeded 270M "
+                              f"model, {threads} host threads"}
+    r = cpu_tokens(shape, threads, 1, 2, prompt)
+    return {"value": r["tok_s"], "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"2 whole decode tokens (after 1 warm-up) of the full {shape.name}-shaped model "
+                      f"({shape.block_count} layers, vocab {shape.vocab_size}) at positions 1-2, C restatement of "
+                      f"src/gemma3.cpp (the reference itself refuses head_count_kv != 1), {threads} host threads; "
+                      f"host model built in {r['create_s']:.0f} s"}
 
 
 def run_reference_arm(args, rank: int, world: int):
+    """The reference's CPU token loop on whole tokens of this workload: one
+    step = one decode token (prompt tokens run through the same loop first for
+    270M; for 27B the 2048-token prefill is not replayed on the host, where it
+    would take about an hour, so the tokens sit at positions 1..K+W)."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    vals = []
-    for _ in range(args.warmup):
-        cpu_baseline(args.workload, threads)
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(args.workload, threads))
-    v = statistics.median([x["value"] for x in vals])
-    cb = dict(vals[-1])
-    cb["value"] = v
-    shape = shape_for(args.workload)
+    workload = args.workload if args.workload in ("27b", "270m", "270m-long") else "27b"
+    shape = shape_for(workload, args.layers, args.vocab)
+    prompt_len = args.prompt_len or PROMPT_LEN[workload]
+    t_all = time.perf_counter()
+    if workload.startswith("270m"):
+        r = cpu_reference_270m(threads, prompt_ids(shape, 8), args.steps, warm=args.warmup)
+        kind, what = "reference", "the reference's own src/gemma3.cpp token loop (oracle/_ref)"
+        pos = "positions 8.."
+    else:
+        r = None
+    if r is None:
+        r = cpu_tokens(shape, threads, args.warmup, args.steps, prompt_ids(shape, 8))
+        kind = "port"
+        what = ("the C restatement of src/gemma3.cpp (oracle/liboracle.so; the reference itself refuses "
+                "head_count_kv != 1)")
+        pos = f"positions {args.warmup}..{args.warmup + args.steps - 1}"
+    v = r["tok_s"]
+    sample = (f"{args.steps} whole greedy decode tokens (after {args.warmup} warm-up tokens) of the full "
+              f"{shape.name}-shaped model, {pos}, {what}, {threads} host threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / v, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "q8_0*f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}-shaped Gemma 3 Q8_0 decode, bs=1", "d_model": shape.embedding_length,
-                   "layers": shape.block_count, "vocab": shape.vocab_size},
-        "cpu_baseline": cb,
+        "config": workload_config(workload, shape, world, prompt_len, args.warmup, args.steps, args.tp_exchange),
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t_all,
     }), flush=True)
+
+
+# ------------------------------------------------------------------ sweep
+
+SWEEP = [("qkv_1920x640_triplet", "multi", 640, 640, 3), ("mv_640x1024", "gemv", 640, 1024, 1),
+         ("ffn_2048x640x2_640x2048", "ffn", 2048, 640, 1), ("lm_262144x640_argmax", "head", 262144, 640, 1),
+         ("mv_21504x5376", "gemv", 21504, 5376, 1)]
+
+
+def sweep(ctx, iters: int = 1000, cpu: bool = True) -> dict:
+    """Config 1: each shape's drop-in pipeline kernel (raw GGUF rows:
+    vrt_q8_gemv[_multi] / vrt_q8_ffn / vrt_lm_head_argmax) and the packed
+    (Q8T) model kernel, `iters` calls each, hot (one weight copy, L2-resident
+    when it fits) and cold (copies rotated over >= 2x L2).  GB/s counts
+    rows*cols/32*34 + 4*cols + 4*rows per call.  With cpu=True the
+    reference's CPU-reference loops are timed on the same shapes (q8_test's
+    fp32 loop, src/q8_test_main.cpp:125-128, and ffn_test's fp64 matvec,
+    src/ffn_test_main.cpp:217-250, both restated in oracle/) and the GPU
+    outputs are checked against the fp64 one (atol/rtol 1e-3)."""
+    import ctypes as Cc
+
+    import torch
+
+    import vrt
+
+    L = vrt.lib()
+    peak, peak_kind = measured_peaks()
+    l2 = ctx.info().l2_bytes
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    out = {"iterations": iters, "peak_gbs": peak, "peak_source": f"{peak_kind} hbm_gbs", "shapes": {}}
+    rng = np.random.default_rng(11)
+    for name, kind, rows, cols, count in SWEEP:
+        if kind == "ffn":
+            mats = [sg.q8_matrix_bytes(SEED, f"sweep.{name}.{t}", r, c) for t, r, c in
+                    (("gate", rows, cols), ("up", rows, cols), ("down", cols, rows))]
+            alg = sum(m.nbytes for m in mats) + 4 * cols + 4 * cols
+        else:
+            mats = [sg.q8_matrix_bytes(SEED, f"sweep.{name}.{i}", rows, cols) for i in range(count)]
+            alg = sum(m.nbytes for m in mats) + 4 * cols + 4 * rows * count + (8 if kind == "head" else 0)
+        raw = np.concatenate(mats)
+        nbytes = raw.nbytes
+        ncopy = max(1, -(-2 * l2 // nbytes))
+        x = rng.standard_normal(cols).astype(np.float32)
+        dev = torch.cuda.current_device()
+        stride = (nbytes + 255) // 256 * 256  # every copy 256-byte aligned
+        w = torch.zeros((ncopy, stride), dtype=torch.uint8, device=dev)
+        w[:, :nbytes] = torch.from_numpy(raw).to(dev)
+        dx = torch.from_numpy(x).to(dev)
+        n_out = (rows * count) if kind != "ffn" else cols
+        dy = torch.zeros(max(n_out, 1), dtype=torch.float32, device=dev)
+        work = torch.zeros(2 * rows, dtype=torch.float32, device=dev)
+        res = torch.zeros(2, dtype=torch.int32, device=dev)
+        offs = (Cc.c_uint64 * count)(*[i * mats[0].nbytes for i in range(count)])
+        dims = (Cc.c_uint32 * count)(*([rows] * count))
+        torch.cuda.synchronize()
+
+        def raw_call(i):
+            base = w[i].data_ptr()
+            if kind == "gemv":
+                return L.vrt_q8_gemv(ctx.h, base, nbytes, 0, dx.data_ptr(), dy.data_ptr(), cols, rows, None)
+            if kind == "multi":
+                return L.vrt_q8_gemv_multi(ctx.h, base, nbytes, offs, dims, count, dx.data_ptr(), dy.data_ptr(), cols,
+                                           None)
+            if kind == "ffn":
+                g, u = mats[0].nbytes, mats[1].nbytes
+                return L.vrt_q8_ffn(ctx.h, base, nbytes, 0, g, g + u, dx.data_ptr(), work.data_ptr(), dy.data_ptr(),
+                                    cols, rows, cols, None)
+            return L.vrt_lm_head_argmax(ctx.h, base, nbytes, 0, dx.data_ptr(), cols, rows, None, res.data_ptr(), None)
+
+        # packed (Q8T) copies of the same matrices, the model kernels' layout
+        if kind == "ffn":
+            pb_gu, pb_dn = L.vrt_q8t_bytes(2 * rows, cols), L.vrt_q8t_bytes(cols, rows)
+            pk = torch.empty((ncopy, pb_gu + pb_dn), dtype=torch.uint8, device=dev)
+            for i in range(ncopy):
+                g, u = mats[0].nbytes, mats[1].nbytes
+                vrt.check(L.vrt_q8t_pack_pair(ctx.h, w[i].data_ptr(), nbytes, 0, g, rows, cols, pk[i].data_ptr(), None))
+                vrt.check(L.vrt_q8t_pack(ctx.h, w[i].data_ptr(), nbytes, g + u, cols, rows,
+                                         pk[i].data_ptr() + pb_gu, None))
+        else:
+            pb = L.vrt_q8t_bytes(rows * count, cols)
+            pk = torch.empty((ncopy, pb), dtype=torch.uint8, device=dev)
+            for i in range(ncopy):
+                vrt.check(L.vrt_q8t_pack(ctx.h, w[i].data_ptr(), nbytes, 0, rows * count, cols, pk[i].data_ptr(), None))
+
+        def packed_call(i):
+            base = pk[i].data_ptr()
+            if kind in ("gemv", "multi"):
+                return L.vrt_q8t_gemv(ctx.h, base, rows * count, cols, dx.data_ptr(), dy.data_ptr(), None)
+            if kind == "ffn":
+                return L.vrt_q8t_ffn(ctx.h, base, base + pb_gu, cols, rows, cols, dx.data_ptr(), work.data_ptr(),
+                                     dy.data_ptr(), None)
+            return L.vrt_q8t_lm_head_argmax(ctx.h, base, rows, cols, dx.data_ptr(), None, res.data_ptr(), None)
+
+        rec = {"rows": rows * count if kind != "ffn" else f"{rows}x2+{cols}", "cols": cols, "bytes_per_call": alg,
+               "weight_copies_cold": ncopy}
+        outputs = {}
+        for label, call in (("raw", raw_call), ("packed", packed_call)):
+            for mode in ("hot", "cold"):
+                for i in range(3):
+                    vrt.check(call(i % ncopy))
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record(stream)
+                for i in range(iters):
+                    call(i % ncopy if mode == "cold" else 0)
+                ev1.record(stream)
+                ev1.synchronize()
+                us = ev0.elapsed_time(ev1) * 1000.0 / iters
+                rec[f"{label}_{mode}_us"] = us
+                rec[f"{label}_{mode}_gbs"] = alg / us / 1e3
+                rec[f"{label}_{mode}_frac"] = alg / us / 1e3 / peak
+            ctx.sync()
+            outputs[label] = (dy.cpu().numpy().copy() if kind != "head" else res.cpu().numpy().copy())
+        if cpu:
+            rec.update(_sweep_cpu(kind, mats, x, rows, cols, count, outputs))
+        out["shapes"][name] = rec
+        del w, pk
+        torch.cuda.empty_cache()
+    return out
+
+
+def _sweep_cpu(kind, mats, x, rows, cols, count, outputs) -> dict:
+    """CPU-reference loops of the reference test programs on the sweep shape
+    (all host threads), and the check of the GPU results against fp64."""
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    rec = {"cpu_threads": threads}
+    if kind == "ffn":
+        t = time.perf_counter()
+        g = O.q8_matvec(mats[0], x, rows, lanes=0, threads=threads)
+        u = O.q8_matvec(mats[1], x, rows, lanes=0, threads=threads)
+        a = O.gelu_mul(g, u)
+        ref = O.q8_matvec(mats[2], a, cols, lanes=0, threads=threads)
+        rec["cpu_ffn_test_fp64_ms"] = (time.perf_counter() - t) * 1e3
+    else:
+        ref = np.concatenate([O.q8_matvec(m, x, rows, lanes=0, threads=threads) for m in mats])
+        t = time.perf_counter()
+        for m in mats:
+            O.q8_matvec(m, x, rows, lanes=0, threads=threads)
+        rec["cpu_ffn_test_fp64_ms"] = (time.perf_counter() - t) * 1e3
+        t = time.perf_counter()
+        for m in mats:
+            O.q8_matvec(m, x, rows, lanes=1, threads=threads)
+        rec["cpu_q8_test_fp32_ms"] = (time.perf_counter() - t) * 1e3
+    if kind == "head":
+        idx, _ = O.argmax(ref)
+        rec["check"] = "argmax equal" if all(int(o[0]) == idx for o in outputs.values()) else "ARGMAX MISMATCH"
+    else:
+        worst = 0.0
+        for o in outputs.values():
+            err = np.abs(o[:ref.size].astype(np.float64) - ref) / (1e-3 + 1e-3 * np.abs(ref))
+            worst = max(worst, float(err.max()))
+        rec["check"] = f"within atol/rtol 1e-3 of fp64 (worst err/bound {worst:.3f})" if worst <= 1 else \
+            f"MISMATCH (err/bound {worst:.3f})"
+    return rec
+
+
+def run_sweep(args):
+    import torch
+
+    import vrt
+
+    ctx = vrt.Context(0)
+    t0 = time.perf_counter()
+    res = sweep(ctx, iters=args.steps if args.steps >= 100 else 1000, cpu=not args.no_cpu_baseline)
+    shapes = res["shapes"]
+    # headline: the largest single mat-vec, cold HBM, packed kernel
+    big = shapes["mv_21504x5376"]
+    line = {"metric": "Q8_0 mat-vec achieved HBM GB/s (21504x5376, cold)", "value": big["packed_cold_gbs"],
+            "unit": "GB/s", "n_gpus": 1, "steps": res["iterations"], "warmup": 3,
+            "ms_per_step": big["packed_cold_us"] / 1000.0, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0*f32", "data": "synthetic (seeded Q8_0 weights, x ~ N(0,1))",
+            "config": {"workload": "config 1: isolated Q8_0 mat-vec / fused FFN / LM head + argmax sweep",
+                       "l2": "cold = weight copies rotated over >= 2x L2; hot = one copy"},
+            "gpu_launches": res["iterations"] * 4 * len(SWEEP),
+            "roofline": {"bound": "hbm", "kernel": "q8t_gemv_kernel (21504x5376, cold)",
+                         "achieved": big["packed_cold_gbs"], "peak": res["peak_gbs"], "unit": "GB/s",
+                         "frac": big["packed_cold_frac"], "traffic": None},
+            "sweep": res, "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+    del torch
+
+
+# ---------------------------------------------------------- decode (bs=1)
+
+def decode_run(args, workload: str, rank: int, world: int, local: int, dist_on: bool, ctx, steps: int, warmup: int,
+               e2e_steps: int, with_margins: bool = True, nccl_id=None) -> dict:
+    """Prefill + timed greedy decode of one model; returns the numbers of the line."""
+    import torch
+    import torch.distributed as dist
+
+    import vrt
+
+    shape = shape_for(workload, args.layers if workload == args.workload else 0,
+                      args.vocab if workload == args.workload else 0)
+    prompt_len = (args.prompt_len if workload == args.workload else 0) or PROMPT_LEN[workload]
+    positions = prompt_len + warmup + steps + e2e_steps + 8
+    prompt = prompt_ids(shape, prompt_len)
+    m = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=SEED, max_positions=positions,
+                  tp_rank=rank, tp_world=world, nccl_id=nccl_id, tp_exchange=args.tp_exchange,
+                  step_mode=args.step_mode)
+    kernels = m.step_kernels()
+    stream = torch.cuda.ExternalStream(ctx.stream)
+
+    def barrier():
+        if dist_on:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        if dist_on:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    barrier()
+    ev[0].record(stream)
+    m.prefill(prompt)
+    ev[1].record(stream)
+    ctx.sync()
+    t_pf = max_over_ranks(ev[0].elapsed_time(ev[1]) / 1000.0)
+
+    m.decode_steps_async(warmup)
+    ctx.sync()
+    tok_start, pos_start = m.next_token()
+    ids_dev = torch.zeros(max(steps, 1), dtype=torch.int32, device="cuda")
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    ctx.sync()
+    barrier()
+    ev[2].record(stream)
+    m.decode_steps_async(steps, ids_dev.data_ptr())
+    ev[3].record(stream)
+    ctx.sync()
+    barrier()
+    clocks = sampler.stop()
+    ms = max_over_ranks(ev[2].elapsed_time(ev[3]))
+    tok_s = steps / (ms / 1000.0)
+    status = m.device_status()
+    ids = ids_dev.cpu().numpy().astype(np.uint32)[:steps]
+    tok, pos = m.next_token()
+
+    # e2e through the C ABI call with host buffers (vrt_decode_step)
+    barrier()
+    ctx.sync()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        _, out_ids, _ = m.decode(tok, pos, 1, want_hidden=False)
+        tok, pos = int(out_ids[0]), pos + 1
+    ctx.sync()
+    e2e_tok_s = e2e_steps / max_over_ranks(time.perf_counter() - t0)
+
+    # the timed steps again, teacher-forced, with top-2 logits: the margins that
+    # tell a legitimate near-tie from a divergence when streams are compared
+    margins = None
+    agree = None
+    if with_margins:
+        m.reset()
+        m.prefill(prompt)
+        m.decode_steps_async(warmup)
+        t, p = m.next_token()
+        assert (t, p) == (tok_start, pos_start)
+        margins, agree = [], 0
+        for i in range(steps):
+            _, top, lg = m.decode(t, p, 2, want_hidden=False)
+            margins.append(float(lg[0] - lg[1]))
+            agree += int(top[0]) == int(ids[i])
+            t, p = int(ids[i]), p + 1
+
+    # dominant kernel alone: layer-0 gate/up mat-vec
+    k_ms, k_bytes = m.time_kernel(0, 2, iters=20)
+    m.close()
+    return {"shape": shape, "prompt_len": prompt_len, "tok_s": tok_s, "ms": ms, "kernels": kernels,
+            "status": status, "clocks": clocks, "e2e": e2e_tok_s, "prefill_s": t_pf, "ids": ids,
+            "margins": margins, "agree": agree, "k_ms": k_ms, "k_bytes": k_bytes}
+
+
+def ids_summary(r: dict) -> dict:
+    ids = r["ids"]
+    out = {"first8": ids[:8].tolist(), "count": int(ids.size),
+           "sha1": hashlib.sha1(ids.astype("<u4").tobytes()).hexdigest()[:16]}
+    if r["margins"] is not None:
+        out["min_top2_margin"] = min(r["margins"]) if r["margins"] else None
+        out["replay_agrees"] = f"{r['agree']}/{ids.size}"
+    return out
+
+
+def line_for(args, workload: str, r: dict, world: int, steps: int, warmup: int, cpu: dict | None) -> dict:
+    peak, peak_kind = measured_peaks()
+    shape = r["shape"]
+    achieved = r["k_bytes"] / (r["k_ms"] / 1000.0) / 1e9
+    step_bytes = bytes_per_token(shape, r["prompt_len"] + warmup + steps // 2)
+    tr = committed_traffic("27b") if workload == "27b" and not args.layers and not args.vocab else None
+    line = {
+        "metric": METRIC, "value": r["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": r["ms"] / steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q8_0*f32", "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
+        "config": workload_config(workload, shape, world, r["prompt_len"], warmup, steps, args.tp_exchange),
+        "gpu_launches": r["kernels"] * steps,
+        "kernels_per_step": r["kernels"],
+        "step_mode": args.step_mode,
+        "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * r["tok_s"] / 1e9 / world,
+                          "peak_gbs": peak, "frac": step_bytes * r["tok_s"] / 1e9 / world / peak,
+                          "note": "per GPU; weights + norms + KV per token over device time"},
+        "roofline": {"bound": "hbm", "kernel": "q8t_gemv_kernel<Resid, GeluPair> (layer gate/up)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": r["k_bytes"],
+                     "ms_per_launch": r["k_ms"],
+                     "traffic": (tr / world) if tr else None,
+                     "traffic_source": ("ncu dram bytes of one 1-GPU launch (profiles/traffic.json)"
+                                        + (f", divided by {world}: each rank streams 1/{world} of the rows"
+                                           if world > 1 else "")) if tr else None},
+        "e2e": {"value": r["e2e"], "unit": "tok/s", "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 40},
+        "prefill": {"tokens": r["prompt_len"], "s": r["prefill_s"], "tok_s": r["prompt_len"] / r["prefill_s"],
+                    "method": "batched: tcgen05 Q8_0 GEMMs + tiled prefill attention, chunks of 2048"
+                              + (", NCCL sums of the row-parallel partials" if world > 1 else "")},
+        "ids": ids_summary(r),
+        "device_status": r["status"],
+        "clocks": r["clocks"],
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="27b", choices=["27b", "270m", "270m-long", "270m-batch", "27b-bs32",
+                                                          "sweep"])
+    ap.add_argument("--prompt-len", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 0 / config 1 results of the default run")
+    ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
+    ap.add_argument("--vocab", type=int, default=0, help="profiling: smaller vocabulary of the same shape")
+    ap.add_argument("--tp-exchange", default="peer", choices=["peer", "nccl"],
+                    help="tensor parallelism: peer-memory exchange fused into the consumer kernels, or NCCL all-reduce")
+    ap.add_argument("--step-mode", default="launches", choices=["launches", "persistent"],
+                    help="decode step as one kernel per op (default) or one persistent kernel per token")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+    if args.workload == "sweep":
+        if rank == 0:
+            run_sweep(args)
+        return None
+    if args.workload in BATCH_SEQS:
+        return run_batched(args, rank, world, local)
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import vrt
+
+    dist_on = world > 1
+    if dist_on:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    nccl_id = None
+    if dist_on:
+        obj = [vrt.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    ctx = vrt.Context(local)
+    e2e_steps = args.steps
+    r = decode_run(args, args.workload, rank, world, local, dist_on, ctx, args.steps, args.warmup, e2e_steps,
+                   nccl_id=nccl_id)
+    extras = {}
+    if world == 1 and args.workload == "27b" and not args.no_extras and not args.layers and not args.vocab:
+        # config 0 on the same GPU in the same run (one GPU: replicas only)
+        r0 = decode_run(args, "270m", 0, 1, local, False, ctx, 256, 8, 64)
+        c0 = line_for(args, "270m", r0, 1, 256, 8, None if args.no_cpu_baseline else
+                      cpu_baseline("270m", r0["shape"], os.cpu_count() or 1))
+        for k in ("metric", "n_gpus", "dtype", "data", "higher_is_better", "vs_baseline", "scaling"):
+            c0.pop(k, None)
+        extras["config0_270m"] = c0
+        # config 1: the isolated kernels
+        extras["config1_sweep"] = sweep(ctx, iters=1000, cpu=not args.no_cpu_baseline)
+    ctx.close()
+    if rank == 0:
+        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, r["shape"], os.cpu_count() or 1)
+        line = line_for(args, args.workload, r, world, args.steps, args.warmup, cpu)
+        if extras:
+            line["also"] = extras
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_batched(args, rank: int, world: int, local: int):
@@ -213,11 +760,7 @@ def run_batched(args, rank: int, world: int, local: int):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     tp = args.workload == "27b-bs32" and world > 1
-    shape = shape_for(args.workload)
-    if args.layers:
-        shape = shape.with_(block_count=args.layers)
-    if args.vocab:
-        shape = shape.with_(vocab_size=args.vocab)
+    shape = shape_for(args.workload, args.layers, args.vocab)
     total = BATCH_SEQS[args.workload]
     M = total if tp else total // world
     prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
@@ -229,7 +772,7 @@ def run_batched(args, rank: int, world: int, local: int):
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     ctx = vrt.Context(local)
-    model = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=1234, max_positions=P,
+    model = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=SEED, max_positions=P,
                       tp_rank=rank if tp else 0, tp_world=world if tp else 1, nccl_id=nccl_id)
     b = vrt.Batch(model, M, P)
     stream = torch.cuda.ExternalStream(ctx.stream)
@@ -278,7 +821,7 @@ def run_batched(args, rank: int, world: int, local: int):
         b.last_ids(M, ids)
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = total * e2e_steps / e2e_s
-    _, pos = b.read(0, 1)
+    first_ids, pos = b.read(0, 1 << 12)
     status = model.device_status()
     b.close()
     model.close()
@@ -291,11 +834,13 @@ def run_batched(args, rank: int, world: int, local: int):
         if tp:
             step_bytes /= world  # per GPU: weights and KV heads are both sharded
         achieved = step_bytes / (ms / 1000.0 / args.steps) / 1e9
-        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, os.cpu_count() or 1)
+        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, shape, os.cpu_count() or 1)
+        seq0 = np.asarray(first_ids, np.uint32)
         line = {
             "metric": METRIC.replace("bs=1", f"batched, {total} sequences"), "value": tok_s, "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q8_0*fp16x2->f32",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "q8_0*int8/fp16->f32",
             "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
             "config": {"workload": {"270m-batch": f"config 3: 270M-shaped Gemma 3 Q8_0, {total} sequences x "
                                                   f"{prompt_len}-token prompts, greedy decode, sequences split over "
@@ -317,176 +862,9 @@ def run_batched(args, rank: int, world: int, local: int):
                     "note": "tokens stay on the device; each step reads back every sequence's new id"},
             "prefill": {"tokens": total * prompt_len, "s": t_pf, "tok_s": total * prompt_len / t_pf,
                         "method": "batched tensor-core prefill per sequence"},
+            "ids": {"sequence0_first8": seq0[:8].tolist(), "sequence0_count": int(seq0.size),
+                    "sequence0_sha1": hashlib.sha1(seq0.astype("<u4").tobytes()).hexdigest()[:16]},
             "final_position": pos,
-            "device_status": status,
-            "clocks": clocks,
-        }
-        if cpu is not None:
-            line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
-    if dist_on:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
-    ap.add_argument("--warmup", type=int, default=4)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="27b", choices=["27b", "270m", "270m-long", "270m-batch", "27b-bs32"])
-    ap.add_argument("--prompt-len", type=int, default=0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
-    ap.add_argument("--vocab", type=int, default=0, help="profiling: smaller vocabulary of the same shape")
-    ap.add_argument("--tp-exchange", default="peer", choices=["peer", "nccl"],
-                    help="tensor parallelism: peer-memory exchange fused into the consumer kernels, or NCCL all-reduce")
-    args = ap.parse_args()
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        return run_reference_arm(args, rank, world)
-
-    import torch
-    import torch.distributed as dist
-
-    import vrt
-
-    if args.workload in BATCH_SEQS:
-        return run_batched(args, rank, world, local)
-
-    dist_on = world > 1
-    if dist_on:
-        torch.cuda.set_device(local)
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    shape = shape_for(args.workload)
-    if args.layers:
-        shape = shape.with_(block_count=args.layers)
-    if args.vocab:
-        shape = shape.with_(vocab_size=args.vocab)
-    prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
-    e2e_steps = args.steps
-    positions = prompt_len + args.warmup + args.steps + e2e_steps + 8
-    prompt = [2] + np.random.default_rng(4).integers(3, shape.vocab_size, prompt_len - 1).tolist()
-
-    nccl_id = None
-    if dist_on:
-        obj = [vrt.tp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
-    ctx = vrt.Context(local)
-    cfg = vrt.Gemma3Config.from_shape(shape)
-    m = vrt.Model(ctx, None, config=cfg, seed=1234, max_positions=positions, tp_rank=rank, tp_world=world,
-                  nccl_id=nccl_id, tp_exchange=args.tp_exchange)
-    kernels = m.step_kernels()
-
-    def barrier():
-        if dist_on:
-            dist.barrier()
-
-    # prefill: batched tensor-core passes (NCCL sums of the row-parallel partials under TP)
-    stream = torch.cuda.ExternalStream(ctx.stream)
-    pf0 = torch.cuda.Event(enable_timing=True)
-    pf1 = torch.cuda.Event(enable_timing=True)
-    barrier()
-    pf0.record(stream)
-    m.prefill(prompt)
-    pf1.record(stream)
-    ctx.sync()
-    t_pf = pf0.elapsed_time(pf1) / 1000.0
-    tpf = torch.tensor([t_pf], dtype=torch.float64, device="cuda")
-    if dist_on:
-        dist.all_reduce(tpf, op=dist.ReduceOp.MAX)
-    t_pf = float(tpf.item())
-
-    # warmup
-    m.decode_steps_async(args.warmup)
-    ctx.sync()
-    barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ctx.sync()
-    barrier()
-    ev0.record(stream)
-    m.decode_steps_async(args.steps)
-    ev1.record(stream)
-    ctx.sync()
-    barrier()
-    clocks = sampler.stop()
-    ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if dist_on:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    tok_s = args.steps / (ms / 1000.0)
-    status = m.device_status()
-    tok, pos = m.next_token()
-
-    # e2e through the C ABI call with host buffers (vrt_decode_step)
-    barrier()
-    ctx.sync()
-    t0 = time.perf_counter()
-    for i in range(e2e_steps):
-        _, ids, _ = m.decode(tok, pos, 1, want_hidden=False)
-        tok, pos = int(ids[0]), pos + 1
-    ctx.sync()
-    e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if dist_on:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_tok_s = e2e_steps / float(te.item())
-
-    # dominant kernel alone: layer-0 gate/up mat-vec
-    k_ms, k_bytes = m.time_kernel(0, 2, iters=20)
-    peak, peak_kind = measured_peaks()
-    achieved = k_bytes / (k_ms / 1000.0) / 1e9
-    step_bytes = bytes_per_token(shape, prompt_len + args.warmup + args.steps // 2)
-    m.close()
-    ctx.close()
-
-    if rank == 0:
-        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, os.cpu_count() or 1)
-        tr = committed_traffic(args.workload)
-        line = {
-            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "q8_0*f32",
-            "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
-            "config": {"workload": {"27b": f"config 4: 27B-shaped Gemma 3 Q8_0, bs=1 greedy decode after a "
-                                           f"{prompt_len}-token prefill",
-                                    "270m": f"config 0: 270M-shaped Gemma 3 Q8_0, bs=1 greedy decode after "
-                                            f"{prompt_len} prompt tokens",
-                                    "270m-long": f"config 2: 270M-shaped Gemma 3 Q8_0, {prompt_len}-token batched "
-                                                 "prefill, then bs=1 greedy decode past the 512-token window"
-                                    }[args.workload],
-                       "d_model": shape.embedding_length, "layers": shape.block_count,
-                       "heads": f"{shape.head_count}q/{shape.head_count_kv}kv x {shape.head_dim}",
-                       "ffn": shape.feed_forward_length, "vocab": shape.vocab_size, "global_batch": 1,
-                       "positions": f"{prompt_len + args.warmup}..{prompt_len + args.warmup + args.steps}",
-                       "parallelism": f"tp{world}" if world > 1 else "single GPU",
-                       "tp_exchange": (("peer memory (partials pushed over NVLink, summed in the consumer kernel)"
-                                        if args.tp_exchange == "peer" else "NCCL all-reduce") if world > 1 else None),
-                       "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB streamed per token)"},
-            "gpu_launches": kernels * args.steps,
-            "kernels_per_step": kernels,
-            "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes * tok_s / 1e9 / world,
-                              "peak_gbs": peak, "frac": step_bytes * tok_s / 1e9 / world / peak,
-                              "note": "per GPU; weights + norms + KV per token over device time"},
-            "roofline": {"bound": "hbm", "kernel": "q8t_gemv_kernel<Resid, GeluPair> (layer gate/up)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": k_bytes,
-                         "ms_per_launch": k_ms, "traffic": tr},
-            "e2e": {"value": e2e_tok_s, "unit": "tok/s", "h2d_bytes_per_step": 20, "d2h_bytes_per_step": 40},
-            "prefill": {"tokens": prompt_len, "s": t_pf, "tok_s": prompt_len / t_pf,
-                        "method": "batched: tcgen05 Q8_0 GEMMs + tiled prefill attention, chunks of 2048"
-                                  + (", NCCL sums of the row-parallel partials" if world > 1 else "")},
             "device_status": status,
             "clocks": clocks,
         }
