@@ -121,9 +121,11 @@ VRT_API int vrt_q8_ffn(vrt_ctx* ctx, const void* d_weights, uint64_t weights_byt
  * loads the library, held until exit), so ffn_dim <= 32768 (larger sizes
  * return VRT_E_INVALID) and nothing is ever allocated.  The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture.  All calls share the one array:
- * calls that overlap on the GPU (other streams, other threads) race on it.
- * `stream` NULL = the CUDA default stream. */
+ * that first call before any stream capture.  That set-up is kept for the
+ * life of the process and is not redone after cudaDeviceReset: do not call
+ * this after resetting a device that it has run on.  All calls share the one
+ * array: calls that overlap on the GPU (other streams, other threads) race on
+ * it.  `stream` NULL = the CUDA default stream. */
 VRT_API int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t gate_off,
                               uint64_t up_off, uint64_t down_off, const float* d_x, float* d_y,
                               uint32_t input_dim, uint32_t ffn_dim, uint32_t output_dim, void* stream);
@@ -291,8 +293,10 @@ VRT_API int vrt_generate_greedy(vrt_model* m, const uint32_t* h_prompt, uint32_t
                                 uint32_t max_new, uint32_t* h_out, uint32_t* h_count);
 
 /* Device-resident continuation for benchmarks: runs `steps` greedy decode steps
- * from the current state (after a prefill), the i-th generated id written to
- * d_out_ids[i] when non-NULL.  No host synchronisation. */
+ * from the current state, the i-th generated id written to d_out_ids[i] when
+ * non-NULL.  No host synchronisation.  Needs a prefill or a decode step with
+ * top_k > 0 first (VRT_E_STATE otherwise): the step state then holds a greedy
+ * id to continue from. */
 VRT_API int vrt_decode_steps_async(vrt_model* m, uint32_t steps, uint32_t* d_out_ids, void* stream);
 
 /* Prefill helper: feeds prompt tokens through the decode step without the LM

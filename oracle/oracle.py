@@ -21,7 +21,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libvrt_ref.so")
-REF_SRC = os.environ.get("VRT_REFERENCE_TREE", "/root/reference")
+# the reference tree: $VRT_REFERENCE_TREE, else the tree beside this repository
+REF_SRC = os.environ.get("VRT_REFERENCE_TREE", os.path.join(os.path.dirname(HERE), "..", "reference"))
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")

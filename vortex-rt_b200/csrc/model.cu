@@ -2077,6 +2077,7 @@ int vrt_decode_step(vrt_model* m, uint32_t token, uint32_t position, uint32_t to
         }
     }
     m->next_pos = position + 1;
+    if (top_k > 0) m->generated = sh->out_count;  // the step emitted a greedy id: device-resident steps may follow
     return VRT_OK;
 }
 
@@ -2131,7 +2132,9 @@ int vrt_prefill(vrt_model* m, const uint32_t* h_prompt, uint32_t n) {
 }
 
 int vrt_decode_steps_async(vrt_model* m, uint32_t steps, uint32_t* d_out_ids, void* stream) {
+    clear_error();
     if (!m) return fail(VRT_E_INVALID, "null model");
+    if (m->generated == 0) return fail(VRT_E_STATE, "decode steps need a prefill (or a decode step) first");
     if (m->next_pos + steps > m->P || m->next_pos + steps > m->cfg.context_length) {
         return fail(VRT_E_STATE, "decode would exceed the KV capacity");
     }
@@ -2467,7 +2470,8 @@ int vrt_batch_create(vrt_model* m, uint32_t max_seqs, uint32_t max_positions, in
         return fail(VRT_E_INVALID, "batch max_positions must be 1..%u (the model's positions)", m->P);
     }
     VRT_CUDA(cudaSetDevice(m->ctx->device));
-    std::unique_ptr<vrt_batch> b(new vrt_batch());
+    // batch_free releases the device memory too when a later step fails
+    std::unique_ptr<vrt_batch, void (*)(vrt_batch*)> b(new vrt_batch(), batch_free);
     b->m = m;
     b->S = max_seqs;
     b->P = max_positions;
