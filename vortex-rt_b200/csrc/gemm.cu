@@ -151,7 +151,7 @@ static cudaError_t gemm_launch_t(const TmaMap& hi, const TmaMap& lo, const GemmP
         if (e != cudaSuccess) return e;
         done |= 1ull << dev;
     }
-    const dim3 grid(p.n / kGemmBN, (p.m + kGemmBM - 1) / kGemmBM);
+    const dim3 grid((p.m + kGemmBM - 1) / kGemmBM, p.n / kGemmBN);  // M tiles fastest (see q8t_gemm_kernel)
     return launch(q8t_gemm_kernel<EPI>, grid, dim3(kGemmThreads), kGemmSmemBytes, s, false, hi, lo, p);
 }
 

@@ -239,7 +239,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t n0 = blockIdx.x * kGemmBN, m0 = blockIdx.y * kGemmBM;
+    // M tiles vary fastest in launch order: the CTAs that share one weight
+    // column run at the same time, so each weight tile leaves HBM once and the
+    // other M tiles read it from L2 (the activations, M x K, stay in L2)
+    const uint32_t m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
     const uint32_t KT = p.k / kTileCols;  // raw stages (128 K columns each)
     const uint32_t NI = 2 * KT;           // operand stages (64 K columns each)
     const uint32_t NC = (NI + kGemmChunkStages - 1) / kGemmChunkStages;  // accumulator chunks
