@@ -1,7 +1,8 @@
 """Tensor parallelism on 2+ B200s: TP=N against TP=1 on the same seeded
 model (hidden states within atol/rtol 1e-3, greedy ids equal unless the TP=1
 top-2 margin is below 1e-3), for the peer-memory exchange (whose ranks must
-also agree bit for bit) and the NCCL one, top-k and full logits gathered
+also agree bit for bit; with the launch chain and with the persistent step
+kernel) and the NCCL one, top-k and full logits gathered
 from the vocabulary shards, batched decode; and the peer exchange's bounded
 wait ending in VRT_E_TIMEOUT when a rank sits out a step.  Skipped on a
 single-GPU box."""
@@ -59,5 +60,12 @@ def test_tp2_batched_decode_matches_single_gpu(shape):
 
 
 @pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
-def test_tp2_peer_wait_times_out():
-    run_worker("tiny-gqa", "peer-timeout")
+@pytest.mark.parametrize("mode", ["peer-timeout", "persistent-timeout"])
+def test_tp2_peer_wait_times_out(mode):
+    run_worker("tiny-gqa", mode)
+
+
+@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("shape", ["tiny-gqa", "27b-slice"])
+def test_tp2_persistent_step_matches_single_gpu(shape):
+    run_worker(shape, "persistent")

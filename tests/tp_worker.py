@@ -14,6 +14,10 @@ Modes:
                   decoded together; ids and per-sequence logits (gathered
                   from the ranks' vocabulary shards) against a single-GPU
                   batch of the same seeded model.
+  persistent   -- as peer, with the decode step as one persistent kernel per
+                  token (VRT_STEP_PERSISTENT): the o-projection / down partial
+                  sums go to every rank's receive area as tagged words
+  persistent-timeout -- as peer-timeout, for the persistent step
   peer-timeout -- failure detection without a GPU fault: after two joint
                   steps rank 1 sits out one step (between steps, nothing in
                   flight); rank 0's exchange waits run out after 1 s and its
@@ -132,8 +136,12 @@ def main():
     cfg = vrt.Gemma3Config.from_shape(shape)
     ctx = vrt.Context(local)
     exchange = "nccl" if mode == "nccl" else "peer"
+    step_mode = "persistent" if mode.startswith("persistent") else "launches"
+    if mode.startswith("persistent"):
+        mode = mode.replace("persistent", "peer")
     m = vrt.Model(ctx, None, config=cfg, seed=seed, max_positions=64, tp_rank=rank, tp_world=world,
-                  nccl_id=obj[0], tp_exchange=exchange, tp_wait_ms=1000 if mode == "peer-timeout" else 0)
+                  nccl_id=obj[0], tp_exchange=exchange, tp_wait_ms=1000 if mode == "peer-timeout" else 0,
+                  step_mode=step_mode)
     toks = [2] + np.random.default_rng(seed).integers(3, shape.vocab_size, 7).tolist()
     ok = True
     if mode == "batch":
