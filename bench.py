@@ -349,7 +349,7 @@ SWEEP = [("qkv_1920x640_triplet", "multi", 640, 640, 3), ("mv_640x1024", "gemv",
          ("mv_21504x5376", "gemv", 21504, 5376, 1)]
 
 
-def sweep(ctx, iters: int = 1000, cpu: bool = True) -> dict:
+def sweep(ctx, iters: int = 1000, cpu: bool = True, only: list[str] | None = None) -> dict:
     """Config 1: each shape's drop-in pipeline kernel (raw GGUF rows:
     vrt_q8_gemv[_multi] / vrt_q8_ffn / vrt_lm_head_argmax) and the packed
     (Q8T) model kernel, `iters` calls each, hot (one weight copy, L2-resident
@@ -372,6 +372,8 @@ def sweep(ctx, iters: int = 1000, cpu: bool = True) -> dict:
     out = {"iterations": iters, "peak_gbs": peak, "peak_source": f"{peak_kind} hbm_gbs", "shapes": {}}
     rng = np.random.default_rng(11)
     for name, kind, rows, cols, count in SWEEP:
+        if only and name not in only:
+            continue
         if kind == "ffn":
             mats = [sg.q8_matrix_bytes(SEED, f"sweep.{name}.{t}", r, c) for t, r, c in
                     (("gate", rows, cols), ("up", rows, cols), ("down", cols, rows))]
@@ -504,10 +506,11 @@ def run_sweep(args):
 
     ctx = vrt.Context(0)
     t0 = time.perf_counter()
-    res = sweep(ctx, iters=args.steps if args.steps >= 100 else 1000, cpu=not args.no_cpu_baseline)
+    only = args.sweep_shapes.split(",") if args.sweep_shapes else None
+    res = sweep(ctx, iters=args.steps if args.steps >= 100 else 1000, cpu=not args.no_cpu_baseline, only=only)
     shapes = res["shapes"]
     # headline: the largest single mat-vec, cold HBM, packed kernel
-    big = shapes["mv_21504x5376"]
+    big = shapes.get("mv_21504x5376") or next(iter(shapes.values()))
     line = {"metric": "Q8_0 mat-vec achieved HBM GB/s (21504x5376, cold)", "value": big["packed_cold_gbs"],
             "unit": "GB/s", "n_gpus": 1, "steps": res["iterations"], "warmup": 3,
             "ms_per_step": big["packed_cold_us"] / 1000.0, "higher_is_better": True, "scaling": "weak",
@@ -678,6 +681,7 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 0 / config 1 results of the default run")
+    ap.add_argument("--sweep-shapes", default="", help="sweep workload: comma-separated subset of the shapes")
     ap.add_argument("--layers", type=int, default=0, help="profiling: fewer layers of the same shape")
     ap.add_argument("--vocab", type=int, default=0, help="profiling: smaller vocabulary of the same shape")
     ap.add_argument("--tp-exchange", default="peer", choices=["peer", "nccl"],

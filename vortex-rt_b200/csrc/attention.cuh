@@ -22,6 +22,9 @@ namespace vrt {
 constexpr int kAttnThreads = 128;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kMaxGroup = 8;   // query heads per KV head handled by one CTA
+// Fewest positions one split takes: a short history runs on few CTAs (up to
+// this many positions on one CTA, with no split merge at all).
+constexpr uint32_t kAttnMinChunk = 32;
 // History splits per KV head are capped at kAttnWarps * head_dim (the merge
 // keeps one weight per split in the warp-merge buffer).
 
@@ -134,7 +137,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     const uint32_t pos = p.pos[z];
     const uint32_t n = p.window ? min(pos + 1, p.window) : pos + 1;
     const uint32_t first = pos + 1 - n;  // oldest position attended
-    const uint32_t chunk = (n + p.splits - 1) / p.splits;
+    // the grid has `splits` CTAs per KV head (sized for the longest history);
+    // the ones past the `used` splits of this position only clear their slice
+    uint32_t chunk = (n + p.splits - 1) / p.splits;
+    if (chunk < kAttnMinChunk) chunk = kAttnMinChunk;
+    const uint32_t used = (n + chunk - 1) / chunk;
     const uint32_t t0 = first + s * chunk;
     const uint32_t t1 = min(first + n, t0 + chunk);
     const float* kc = k_cache + static_cast<uint64_t>(g) * p.cap * hd;
@@ -150,6 +157,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
         const uint32_t a1 = static_cast<uint64_t>(p.zero0_count) * (b + 1) / nb;
         for (uint32_t i = a0 + tid; i < a1; i += kAttnThreads) p.zero0[i] = 0.0f;
     }
+    if (s >= used) return;
     const float* cs = p.rope_cos + static_cast<uint64_t>(pos) * (hd / 2);
     const float* sn = p.rope_sin + static_cast<uint64_t>(pos) * (hd / 2);
 
@@ -275,6 +283,23 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
             for (int m = 0; m < M; ++m) a[m] = fmaf(w_acc[w][r][lane + 32 * m], f, a[m]);
         }
         const uint32_t h = g * R + r;
+        if (used == 1) {  // the whole history in this CTA: the output directly
+            const float inv = 1.0f / L_;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const float v = a[m] * inv;
+                const uint64_t o = static_cast<uint64_t>(h) * hd + lane + 32 * m;
+                if (out_hi) {
+                    __half hh, ll;
+                    split_f16(v, hh, ll);
+                    out_hi[o] = hh;
+                    out_lo[o] = ll;
+                } else {
+                    out[o] = v;
+                }
+            }
+            continue;
+        }
         float* pa = part_acc + (static_cast<uint64_t>(h) * p.splits + s) * hd;
 #pragma unroll
         for (int m = 0; m < M; ++m) pa[lane + 32 * m] = a[m];
@@ -283,11 +308,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
             part_ml[(static_cast<uint64_t>(h) * p.splits + s) * 2 + 1] = L_;
         }
     }
+    if (used == 1) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) {
         const uint32_t ticket = atomicAdd(tickets + g, 1u);
-        last_flag = (ticket == p.splits - 1) ? 1u : 0u;
+        last_flag = (ticket == used - 1) ? 1u : 0u;
     }
     __syncthreads();
     if (!last_flag) return;
@@ -295,7 +321,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     // 4. merge the splits that saw positions, in split order: split maxima
     //    and weights one split per lane, then the accumulators with eight
     //    splits' loads in flight per lane
-    const uint32_t used = min(p.splits, (n + chunk - 1) / chunk);
     for (uint32_t r = warp; r < R; r += kAttnWarps) {
         const uint32_t h = g * R + r;
         const float* ml = part_ml + static_cast<uint64_t>(h) * p.splits * 2;
