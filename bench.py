@@ -35,8 +35,9 @@ Printed JSON line (rank 0):
   prefill        the prompt's prefill, device-timed, tokens/s
   clocks         SM clock / throttle reasons sampled in-process (NVML, 10 ms)
                  during the timed region
-  also           (default workload, one GPU) config 0 and the config 1 sweep,
-                 measured in the same run
+  also           (default workload) configs 0, 1, 2 and 4 at batch 32 on one
+                 GPU, and config 3 at every N (its sequences split over the
+                 ranks as replicas), measured in the same run
 `--impl reference` runs the reference arm: the reference's CPU token loop
 (oracle/_ref for the 270M shape; the C restatement of it where the reference
 refuses the shape, e.g. 16 KV heads) on whole tokens of the same workload.
@@ -670,6 +671,16 @@ def line_for(args, workload: str, r: dict, world: int, steps: int, warmup: int, 
     return line
 
 
+def also_line(line: dict | None) -> dict | None:
+    """A secondary workload's line inside the default line's `also`: the keys
+    that repeat the main line's are dropped, the rest is kept as printed."""
+    if line is None:
+        return None
+    for k in ("metric", "n_gpus", "dtype", "data", "higher_is_better", "vs_baseline"):
+        line.pop(k, None)
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -724,16 +735,25 @@ def main():
     r = decode_run(args, args.workload, rank, world, local, dist_on, ctx, args.steps, args.warmup, e2e_steps,
                    nccl_id=nccl_id)
     extras = {}
-    if world == 1 and args.workload == "27b" and not args.no_extras and not args.layers and not args.vocab:
+    extras_on = args.workload == "27b" and not args.no_extras and not args.layers and not args.vocab
+    if world == 1 and extras_on:
         # config 0 on the same GPU in the same run (one GPU: replicas only)
         r0 = decode_run(args, "270m", 0, 1, local, False, ctx, 256, 8, 64)
         c0 = line_for(args, "270m", r0, 1, 256, 8, None if args.no_cpu_baseline else
                       cpu_baseline("270m", r0["shape"], os.cpu_count() or 1))
-        for k in ("metric", "n_gpus", "dtype", "data", "higher_is_better", "vs_baseline", "scaling"):
-            c0.pop(k, None)
-        extras["config0_270m"] = c0
+        extras["config0_270m"] = also_line(c0)
         # config 1: the isolated kernels
         extras["config1_sweep"] = sweep(ctx, iters=1000, cpu=not args.no_cpu_baseline)
+        # config 2: 4096-token batched prefill, then decode past the 512 window
+        r2 = decode_run(args, "270m-long", 0, 1, local, False, ctx, 512, 8, 32)
+        extras["config2_270m_long"] = also_line(line_for(args, "270m-long", r2, 1, 512, 8, None))
+        # config 4 at batch 32 (one GPU; under torchrun the default line is the bs=1 tensor-parallel one)
+        extras["config4_bs32"] = also_line(batched_run(args, "27b-bs32", 0, 1, local, False, ctx, 16, 3))
+    if extras_on:
+        # config 3 on every rank: the 256 sequences split over the ranks as replicas, no collective
+        r3 = batched_run(args, "270m-batch", rank, world, local, dist_on, ctx, 64, 4)
+        if r3 is not None:
+            extras["config3_270m_batch"] = also_line(r3)
     ctx.close()
     if rank == 0:
         cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, r["shape"], os.cpu_count() or 1)
@@ -747,11 +767,7 @@ def main():
 
 
 def run_batched(args, rank: int, world: int, local: int):
-    """Configs 3 / 4-bs32: independent sequences decoded together (vrt_batch).
-    Under torchrun, config 3 splits the sequences evenly over the ranks, each
-    rank a full replica with no collective on the data path ("replicas");
-    config 4 at batch 32 is tensor parallel (every rank holds all sequences
-    and 1/N of every projection, NCCL all-reduce after o-proj and down)."""
+    """`--workload 270m-batch` / `27b-bs32` on their own."""
     import datetime
 
     import torch
@@ -763,19 +779,43 @@ def run_batched(args, rank: int, world: int, local: int):
     if dist_on:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
-    tp = args.workload == "27b-bs32" and world > 1
-    shape = shape_for(args.workload, args.layers, args.vocab)
-    total = BATCH_SEQS[args.workload]
+    ctx = vrt.Context(local)
+    line = batched_run(args, args.workload, rank, world, local, dist_on, ctx, args.steps, args.warmup,
+                       cpu=not args.no_cpu_baseline)
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def batched_run(args, workload: str, rank: int, world: int, local: int, dist_on: bool, ctx, steps: int,
+                warmup: int, cpu: bool = False) -> dict | None:
+    """Configs 3 / 4-bs32: independent sequences decoded together (vrt_batch).
+    Under torchrun, config 3 splits the sequences evenly over the ranks, each
+    rank a full replica with no collective on the data path ("replicas");
+    config 4 at batch 32 is tensor parallel (every rank holds all sequences
+    and 1/N of every projection, NCCL all-reduce after o-proj and down).
+    Returns the line on rank 0 (None elsewhere); every rank must call."""
+    import torch
+    import torch.distributed as dist
+
+    import vrt
+
+    own = workload == args.workload
+    tp = workload == "27b-bs32" and world > 1
+    shape = shape_for(workload, args.layers if own else 0, args.vocab if own else 0)
+    total = BATCH_SEQS[workload]
     M = total if tp else total // world
-    prompt_len = args.prompt_len or PROMPT_LEN[args.workload]
-    e2e_steps = max(4, args.steps // 4)
-    P = prompt_len + args.warmup + args.steps + e2e_steps + 8
+    prompt_len = (args.prompt_len if own else 0) or PROMPT_LEN[workload]
+    e2e_steps = max(4, steps // 4)
+    P = prompt_len + warmup + steps + e2e_steps + 8
     nccl_id = None
     if tp:
         obj = [vrt.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
-    ctx = vrt.Context(local)
     model = vrt.Model(ctx, None, config=vrt.Gemma3Config.from_shape(shape), seed=SEED, max_positions=P,
                       tp_rank=rank if tp else 0, tp_world=world if tp else 1, nccl_id=nccl_id)
     b = vrt.Batch(model, M, P)
@@ -800,7 +840,7 @@ def run_batched(args, rank: int, world: int, local: int):
     ev[1].record(stream)
     ctx.sync()
     t_pf = max_over_ranks(ev[0].elapsed_time(ev[1]) / 1000.0)
-    b.decode_steps(M, args.warmup)
+    b.decode_steps(M, warmup)
     ctx.sync()
     barrier()
     sampler = ClockSampler(local)
@@ -808,13 +848,13 @@ def run_batched(args, rank: int, world: int, local: int):
     ctx.sync()
     barrier()
     ev[2].record(stream)
-    b.decode_steps(M, args.steps)
+    b.decode_steps(M, steps)
     ev[3].record(stream)
     ctx.sync()
     barrier()
     clocks = sampler.stop()
     ms = max_over_ranks(ev[2].elapsed_time(ev[3]))
-    tok_s = total * args.steps / (ms / 1000.0)
+    tok_s = total * steps / (ms / 1000.0)
     # e2e: the public call per step plus the read-back of every sequence's new id
     ids = np.zeros(M, np.uint32)
     barrier()
@@ -829,55 +869,52 @@ def run_batched(args, rank: int, world: int, local: int):
     status = model.device_status()
     b.close()
     model.close()
-    ctx.close()
-    if rank == 0:
-        peak, peak_kind = measured_peaks()
-        mid = prompt_len + args.warmup + args.steps // 2
-        weights = bytes_per_token(shape, 0)  # weights + norms (+ one position of KV)
-        step_bytes = weights + M * (bytes_per_token(shape, mid) - weights)
-        if tp:
-            step_bytes /= world  # per GPU: weights and KV heads are both sharded
-        achieved = step_bytes / (ms / 1000.0 / args.steps) / 1e9
-        cpu = None if args.no_cpu_baseline else cpu_baseline(args.workload, shape, os.cpu_count() or 1)
-        seq0 = np.asarray(first_ids, np.uint32)
-        line = {
-            "metric": METRIC.replace("bs=1", f"batched, {total} sequences"), "value": tok_s, "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
-            "dtype": "q8_0*int8/fp16->f32",
-            "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
-            "config": {"workload": {"270m-batch": f"config 3: 270M-shaped Gemma 3 Q8_0, {total} sequences x "
-                                                  f"{prompt_len}-token prompts, greedy decode, sequences split over "
-                                                  f"{world} replica(s)",
-                                    "27b-bs32": f"config 4 at batch {total}: 27B-shaped, {prompt_len}-token prompts"
-                                                + (f", tensor parallel over {world} GPUs" if tp else "")
-                                    }[args.workload],
-                       "d_model": shape.embedding_length, "layers": shape.block_count, "vocab": shape.vocab_size,
-                       "global_batch": total, "sequences_per_gpu": M,
-                       "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1 else "single GPU",
-                       "positions": f"{prompt_len + args.warmup}..{prompt_len + args.warmup + args.steps}",
-                       "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB per step)"},
-            "gpu_launches": (7 * shape.block_count + 3) * args.steps,
-            "kernels_per_step": 7 * shape.block_count + 3,
-            "roofline": {"bound": "hbm", "kernel": "whole batched step: Q8_0 weights once + every sequence's KV",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_step": step_bytes, "traffic": None},
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4 * M,
-                    "note": "tokens stay on the device; each step reads back every sequence's new id"},
-            "prefill": {"tokens": total * prompt_len, "s": t_pf, "tok_s": total * prompt_len / t_pf,
-                        "method": "batched tensor-core prefill per sequence"},
-            "ids": {"sequence0_first8": seq0[:8].tolist(), "sequence0_count": int(seq0.size),
-                    "sequence0_sha1": hashlib.sha1(seq0.astype("<u4").tobytes()).hexdigest()[:16]},
-            "final_position": pos,
-            "device_status": status,
-            "clocks": clocks,
-        }
-        if cpu is not None:
-            line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
-    if dist_on:
-        dist.barrier()
-        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_peaks()
+    mid = prompt_len + warmup + steps // 2
+    weights = bytes_per_token(shape, 0)  # weights + norms (+ one position of KV)
+    step_bytes = weights + M * (bytes_per_token(shape, mid) - weights)
+    if tp:
+        step_bytes /= world  # per GPU: weights and KV heads are both sharded
+    achieved = step_bytes / (ms / 1000.0 / steps) / 1e9
+    cpu_line = cpu_baseline(workload, shape, os.cpu_count() or 1) if cpu else None
+    seq0 = np.asarray(first_ids, np.uint32)
+    line = {
+        "metric": METRIC.replace("bs=1", f"batched, {total} sequences"), "value": tok_s, "unit": "tok/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": "q8_0*int8/fp16->f32",
+        "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
+        "config": {"workload": {"270m-batch": f"config 3: 270M-shaped Gemma 3 Q8_0, {total} sequences x "
+                                              f"{prompt_len}-token prompts, greedy decode, sequences split over "
+                                              f"{world} replica(s)",
+                                "27b-bs32": f"config 4 at batch {total}: 27B-shaped, {prompt_len}-token prompts"
+                                            + (f", tensor parallel over {world} GPUs" if tp else "")
+                                }[workload],
+                   "d_model": shape.embedding_length, "layers": shape.block_count, "vocab": shape.vocab_size,
+                   "global_batch": total, "sequences_per_gpu": M,
+                   "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1 else "single GPU",
+                   "positions": f"{prompt_len + warmup}..{prompt_len + warmup + steps}",
+                   "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB per step)"},
+        "gpu_launches": (7 * shape.block_count + 3) * steps,
+        "kernels_per_step": 7 * shape.block_count + 3,
+        "roofline": {"bound": "hbm", "kernel": "whole batched step: Q8_0 weights once + every sequence's KV",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_step": step_bytes, "traffic": None},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4 * M,
+                "note": "tokens stay on the device; each step reads back every sequence's new id"},
+        "prefill": {"tokens": total * prompt_len, "s": t_pf, "tok_s": total * prompt_len / t_pf,
+                    "method": "batched tensor-core prefill per sequence"},
+        "ids": {"sequence0_first8": seq0[:8].tolist(), "sequence0_count": int(seq0.size),
+                "sequence0_sha1": hashlib.sha1(seq0.astype("<u4").tobytes()).hexdigest()[:16]},
+        "final_position": pos,
+        "device_status": status,
+        "clocks": clocks,
+    }
+    if cpu_line is not None:
+        line["cpu_baseline"] = cpu_line
+    return line
 
 
 if __name__ == "__main__":
