@@ -146,6 +146,15 @@ VRT_API int vrt_lm_head_argmax(vrt_ctx* ctx, const void* d_weights, uint64_t wei
                                uint32_t vocab, float* d_logits, vrt_argmax_result* d_out,
                                void* stream);
 
+/* Device error word of the pipeline entry points above (bit 0: a bounded
+ * wait of the staged mat-vec kernel for its own bulk copy gave up, after
+ * about a second; that call's outputs are then undefined), read and cleared.
+ * ctx != NULL: the context's calls (its stream is synchronised first);
+ * ctx == NULL: vrt_q8_ffn_static's calls on the current device (synchronise
+ * the stream they ran on first).  No counterpart in the reference, whose
+ * shaders have no waits. */
+VRT_API int vrt_pipeline_status(vrt_ctx* ctx, uint32_t* h_status);
+
 /* --------------------------------------- packed (Q8T) fast path
  * The model's own weight layout, exposed for callers that keep a matrix
  * resident and call it many times: rows of 16 x 128-column tiles, each tile's

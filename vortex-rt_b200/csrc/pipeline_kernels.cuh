@@ -3,7 +3,10 @@
 // aligned offset, the layout Q8MatVecPipeline::run consumes
 // (src/q8_matvec.cpp:801-930).
 //
-// Row mapping: G lanes per row (G = 8/16/32 by row width), rows grid-strided.
+// Two kernels: the staged one further down (rows of up to 1024 blocks, the
+// default) and this row-wise one (wider rows, or VRT_RAW_ROWWISE=1).
+//
+// Row-wise form.  Row mapping: G lanes per row (G = 8/16/32 by row width), rows grid-strided.
 // A lane reads each of its blocks with aligned 32-bit loads and realigns
 // the quants with funnel shifts (a block starts 2 bytes off a word boundary
 // in every other position); no read leaves the block's own bytes and the
@@ -159,6 +162,346 @@ __global__ void __launch_bounds__(kRawThreads) raw_gemv_kernel(const RawGemvPara
         if (threadIdx.x == 0) {
             unsigned long long b = 0ull;
             for (uint32_t w = 0; w < blockDim.x / 32; ++w) b = warp_best[w] > b ? warp_best[w] : b;
+            if (b) atomicMax(p.amax, b);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Staged form (the default for input_dim <= 32768).  The kernel above reads
+// every 34-byte block with nine 4-byte loads spread over 32 lanes, which
+// keeps L1 busy with ~9 wavefronts per useful sector.  Here each CTA owns a
+// contiguous run of rows of ONE matrix and walks it in iterations of
+// U * 512 / LPR rows:
+//   * copy: a producer warp moves each iteration's bytes into a shared-memory
+//     ring slot with ONE 1-D bulk copy of the window [floor128(first byte),
+//     ceil128(last byte)), clipped to the 16-byte chunks that lie inside the
+//     matrix, and refills a slot as soon as all 16 consumer warps have
+//     released it (per-slot full/empty mbarriers; the consumer warps never
+//     wait for one another).  The at most two blocks that touch a chunk
+//     straddling the matrix's first or last byte are read from global memory
+//     with the aligned in-block loads of the kernel above.
+//   * compute: consumer thread t serves column blocks t % LPR (+ LPR) of row
+//     slots t / LPR (+ 512 / LPR) and keeps those blocks' activations in
+//     registers for the whole kernel, quantised once to an int16 digit plus
+//     an int8 digit, x ~= s * (hi + lo / 256), s = amax / 32767: about 24
+//     bits of the block maximum (the reference FFN test's outputs, up to
+//     ~470, stay within 4e-5 of fp64 against its 5e-3 tolerance).  Block sums
+//     are exact dp2a / dp4a integer sums per digit.
+//   * reduce: a shuffle tree over the row's LPR lanes; for LPR > 32 the warp
+//     sums go to shared memory and the last of the row's warps to arrive adds
+//     them in warp order.  Fixed order: results replay bit for bit.
+// Every mbarrier wait is bounded; an expired wait sets kStatusWaitTimeout in
+// `status` and ends the walk, and the producer waits (bounded again) for the
+// copies still in flight before the CTA exits.
+// ---------------------------------------------------------------------------
+constexpr int kRawStagedThreads = 512;          // consumer threads; + 1 producer warp
+constexpr uint32_t kRawStagedMaxBlocks = 1024;  // NB = 2 blocks per thread at LPR = 512
+constexpr uint32_t kRawStagedMaxSlots = 10;
+// Copy windows start and end on 128-byte boundaries (whole L2 lines; the ring
+// slots are multiples of 128 bytes), clipped to the matrix's 16-byte chunks
+// at its two ends.
+constexpr uint32_t kRawWindowAlign = 128;
+
+struct RawStagedParams {
+    const uint8_t* w;
+    uint64_t offsets[kMaxMulti];
+    uint32_t row_start[kMaxMulti + 1];  // prefix sums of output dims
+    uint32_t cta_start[kMaxMulti + 1];  // prefix sums of CTAs per matrix
+    uint32_t count;
+    uint32_t cols;
+    const float* x;
+    float* y;
+    unsigned long long* amax;
+    uint32_t* status;     // kStatusWaitTimeout on an expired wait (may be null)
+    uint32_t slot_bytes;  // one ring slot (multiple of 128)
+    uint32_t slots;       // ring slots (3..kRawStagedMaxSlots), all kept in flight
+};
+
+// The 9 aligned words covering a block at byte address a (a % 4 in {0, 2})
+// straight from global memory, every read inside [a - 2, a + 34) as in
+// raw_gemv_kernel; returns the quants realigned and the scale bits.
+__device__ __forceinline__ uint32_t raw_block_global(const uint8_t* a, uint32_t (&q)[8]) {
+    const bool odd = (reinterpret_cast<uintptr_t>(a) & 3u) != 0u;
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(a - (odd ? 2 : 0));
+    uint32_t W[9];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) W[i] = __ldg(wp + i);
+    W[8] = odd ? __ldg(wp + 8) : static_cast<uint32_t>(__ldg(reinterpret_cast<const uint16_t*>(a + 32)));
+    if (odd) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = W[i + 1];
+        return W[0] >> 16;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(W[i], W[i + 1], 16);
+    return W[0] & 0xffffu;
+}
+
+// Same from a shared-memory copy whose window starts on a 16-byte boundary
+// (so the block's offset in it has the block's address alignment), without a
+// branch on that alignment (neighbouring lanes hold blocks of both parities):
+// the quants start at off + 2, read as 9 words from floor((off + 2) / 4) and
+// realigned by a funnel shift of 0 or 16 bits; the scale is one 16-bit load.
+// Reads reach at most 4 bytes past the block (the slot has that slack).
+__device__ __forceinline__ uint32_t raw_block_smem(const uint8_t* slot, uint32_t off, uint32_t (&q)[8]) {
+    const uint32_t qb = off + 2u;
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(slot + (qb & ~3u));
+    const uint32_t sh = (qb & 3u) * 8u;
+    uint32_t W[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) W[i] = wp[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(W[i], W[i + 1], sh);
+    return *reinterpret_cast<const uint16_t*>(slot + off);
+}
+
+template <int LPR, int NB, int U>
+__global__ void __launch_bounds__(kRawStagedThreads + 32, 1) raw_gemv_staged_kernel(const RawStagedParams p) {
+    constexpr uint32_t RPI0 = kRawStagedThreads / LPR;  // row slots
+    constexpr uint32_t RPI = U * RPI0;                  // rows per iteration
+    constexpr uint32_t WPR = LPR >= 32 ? LPR / 32 : 1;  // warps per row
+    constexpr uint32_t NW = kRawStagedThreads / 32;     // consumer warps
+    extern __shared__ __align__(128) uint8_t ring[];
+    // LPR > 32: warp partial sums and arrival counts per (ring slot, row)
+    __shared__ float red[LPR > 32 ? kRawStagedMaxSlots : 1][U][NW];
+    __shared__ uint32_t red_count[LPR > 32 ? kRawStagedMaxSlots : 1][U][RPI0];
+    __shared__ unsigned long long warp_best[NW];
+    __shared__ __align__(8) uint64_t full[kRawStagedMaxSlots];
+    __shared__ __align__(8) uint64_t empty[kRawStagedMaxSlots];
+    __shared__ uint32_t abort_flag;
+
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t nblk = p.cols / 32;
+    const uint32_t rb = nblk * 34u;
+    // this CTA's matrix and rows
+    uint32_t m = 0;
+    while (m + 1 < p.count && blockIdx.x >= p.cta_start[m + 1]) ++m;
+    const uint32_t k = blockIdx.x - p.cta_start[m], cnt = p.cta_start[m + 1] - p.cta_start[m];
+    const uint32_t rows_m = p.row_start[m + 1] - p.row_start[m];
+    const uint32_t ra = static_cast<uint32_t>(static_cast<uint64_t>(rows_m) * k / cnt);
+    const uint32_t rb_end = static_cast<uint32_t>(static_cast<uint64_t>(rows_m) * (k + 1) / cnt);
+    const uint32_t n_iter = (rb_end - ra + RPI - 1) / RPI;
+    const uintptr_t mstart = reinterpret_cast<uintptr_t>(p.w + p.offsets[m]);
+    const uintptr_t mend = mstart + static_cast<uint64_t>(rows_m) * rb;
+    const uintptr_t cstart = (mstart + 15) & ~static_cast<uintptr_t>(15);  // copyable chunks: [cstart, cend)
+    const uintptr_t cend = mend & ~static_cast<uintptr_t>(15);
+    const uint32_t NS = p.slots;
+
+    auto row_addr = [&](uint32_t r) -> uintptr_t { return mstart + static_cast<uint64_t>(r) * rb; };
+    auto aborted = [&]() { return *reinterpret_cast<volatile uint32_t*>(&abort_flag) != 0u; };
+    auto fail = [&]() {
+        if (p.status) atomicOr(p.status, kStatusWaitTimeout);
+        abort_flag = 1u;
+    };
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        fence_mbar_init();
+        abort_flag = 0u;
+    }
+    if (LPR > 32) {
+        for (uint32_t i = tid; i < sizeof(red_count) / 4; i += blockDim.x) (&red_count[0][0][0])[i] = 0u;
+    }
+    __syncthreads();  // barriers and counters initialised
+
+    if (warp == NW) {
+        // ---------------------------------------------------- producer warp
+        // weights do not depend on the previous kernel: this warp never waits
+        // for it, and refills each slot as soon as all consumer warps released
+        // it (their release-arrivals on empty[] order their reads of the slot
+        // before the copy's writes)
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();  // weights are read once
+            uint32_t issued_n = 0;
+            for (uint32_t j = 0; j < n_iter; ++j) {
+                if (j >= NS && !mbar_wait_bounded(&empty[j % NS], ((j / NS) - 1) & 1u)) fail();
+                if (aborted()) break;
+                const uint32_t r0 = ra + j * RPI, r1 = min(r0 + RPI, rb_end);
+                const uintptr_t lo = row_addr(r0) & ~static_cast<uintptr_t>(kRawWindowAlign - 1);
+                const uintptr_t hi =
+                    (row_addr(r1) + kRawWindowAlign - 1) & ~static_cast<uintptr_t>(kRawWindowAlign - 1);
+                const uintptr_t c0 = lo > cstart ? lo : cstart, c1 = hi < cend ? hi : cend;
+                uint64_t* bar = &full[j % NS];
+                if (c1 > c0) {
+                    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(c1 - c0));
+                    bulk_copy_g2s_hint(ring + (j % NS) * p.slot_bytes + (c0 - lo), reinterpret_cast<const void*>(c0),
+                                       static_cast<uint32_t>(c1 - c0), bar, pol);
+                } else {
+                    mbar_arrive(bar);
+                }
+                issued_n = j + 1;
+            }
+            if (aborted()) {
+                // copies in flight: wait for them (bounded) before the CTA's shared memory is released
+                for (uint32_t j = issued_n > NS ? issued_n - NS : 0u; j < issued_n; ++j) {
+                    mbar_wait_bounded(&full[j % NS], (j / NS) & 1u);
+                }
+            }
+        }
+        return;
+    }
+
+    // --------------------------------------------------------- consumers
+    pdl_wait();
+    const uint32_t rs = tid / LPR, c0 = tid % LPR;
+    uint32_t xh[NB][16], xl[NB][8];
+    float sx[NB];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+        const uint32_t b = c0 + nb * LPR;
+        sx[nb] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xh[nb][j] = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xl[nb][j] = 0u;
+        if (b < nblk) {
+            float v[32];
+            if ((reinterpret_cast<uintptr_t>(p.x) & 15u) == 0u) {  // one 128-byte line per thread
+                const float4* src = reinterpret_cast<const float4*>(p.x + b * 32);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 f = __ldg(src + j);
+                    v[4 * j] = f.x, v[4 * j + 1] = f.y, v[4 * j + 2] = f.z, v[4 * j + 3] = f.w;
+                }
+            } else {  // x need only be 4-byte aligned
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = __ldg(p.x + b * 32 + e);
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(v[e]));
+            const float sc = quant_scale(amax);
+            sx[nb] = sc;
+            const float inv = amax > 0.0f ? 32767.0f / amax : 0.0f;
+            const float inv_lo = inv * 256.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                int q[4], r[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const float xv = v[4 * j + h];
+                    q[h] = quant_one(xv, inv);
+                    const int rr = __float2int_rn(fmaf(-static_cast<float>(q[h]), sc, xv) * inv_lo);
+                    r[h] = rr > 127 ? 127 : (rr < -127 ? -127 : rr);
+                }
+                xh[nb][2 * j] = (static_cast<uint32_t>(q[0]) & 0xffffu) | (static_cast<uint32_t>(q[1]) << 16);
+                xh[nb][2 * j + 1] = (static_cast<uint32_t>(q[2]) & 0xffffu) | (static_cast<uint32_t>(q[3]) << 16);
+                xl[nb][j] = (static_cast<uint32_t>(r[0]) & 0xffu) | ((static_cast<uint32_t>(r[1]) & 0xffu) << 8) |
+                            ((static_cast<uint32_t>(r[2]) & 0xffu) << 16) | (static_cast<uint32_t>(r[3]) << 24);
+            }
+        }
+    }
+    pdl_trigger();
+
+    unsigned long long best = 0ull;
+    auto emit = [&](uint32_t row, float v) {
+        const uint32_t out = p.row_start[m] + row;
+        if (p.y) p.y[out] = v;
+        if (p.amax && !isnan(v)) {
+            const unsigned long long key = argmax_key(v, out);
+            best = key > best ? key : best;
+        }
+    };
+
+    for (uint32_t it = 0; it < n_iter; ++it) {
+        if (aborted()) break;
+        const uint32_t slot_i = it % NS;
+        if (!mbar_wait_bounded(&full[slot_i], (it / NS) & 1u)) fail();
+        if (aborted()) break;
+        const uint8_t* slot = ring + slot_i * p.slot_bytes;
+        const uint32_t r0 = ra + it * RPI;
+        const uintptr_t a0 = row_addr(r0);
+        const uint32_t mis = static_cast<uint32_t>(a0 & (kRawWindowAlign - 1));  // iteration start in its window
+        // only an iteration holding the matrix's first or last row can meet an uncopied chunk
+        const bool edge_it = (r0 == 0 && mstart != cstart) || (r0 + RPI >= rows_m && mend != cend);
+        float acc[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            acc[u] = 0.0f;
+            const uint32_t rr = u * RPI0 + rs;  // row within the iteration
+            if (r0 + rr < rb_end) {
+#pragma unroll
+                for (int nb = 0; nb < NB; ++nb) {
+                    const uint32_t b = c0 + nb * LPR;
+                    if (b < nblk) {
+                        const uint32_t off = mis + rr * rb + 34u * b;
+                        uint32_t q[8], sb;
+                        bool global_read = false;
+                        if (edge_it) {
+                            const uintptr_t a_lo = (a0 + rr * rb + 34u * b) & ~static_cast<uintptr_t>(3);
+                            global_read = (a_lo & ~static_cast<uintptr_t>(15)) < cstart ||
+                                          ((a_lo + 36u + 15u) & ~static_cast<uintptr_t>(15)) > cend;
+                        }
+                        if (global_read) {
+                            sb = raw_block_global(reinterpret_cast<const uint8_t*>(a0 + off - mis), q);
+                        } else {
+                            sb = raw_block_smem(slot, off, q);
+                        }
+                        // three independent integer chains (even pairs, odd pairs, low digit)
+                        int s0 = 0, s1 = 0, sl = 0;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            s0 = __dp2a_lo(static_cast<int>(xh[nb][2 * i]), static_cast<int>(q[i]), s0);
+                            s1 = __dp2a_hi(static_cast<int>(xh[nb][2 * i + 1]), static_cast<int>(q[i]), s1);
+                            sl = __dp4a(static_cast<int>(xl[nb][i]), static_cast<int>(q[i]), sl);
+                        }
+                        const float blockv = fmaf(static_cast<float>(sl), 1.0f / 256.0f, static_cast<float>(s0 + s1));
+                        acc[u] += __fmul_rn(half_bits_to_float(sb), sx[nb]) * blockv;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int o = (LPR < 32 ? LPR : 32) / 2; o > 0; o >>= 1) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], o);
+        }
+        if (LPR <= 32) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t row = r0 + u * RPI0 + rs;
+                if (c0 == 0 && row < rb_end) emit(row, acc[u]);
+            }
+        } else if (lane == 0) {
+            // the last of the row's WPR warps to arrive adds the partials in warp order
+            const uint32_t wr = warp % WPR;  // this warp's place in its row
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                red[slot_i][u][warp] = acc[u];
+                __threadfence_block();
+                const uint32_t prev = atomicAdd(&red_count[slot_i][u][rs], 1u);
+                if (prev == WPR - 1) {
+                    __threadfence_block();
+                    const uint32_t row = r0 + u * RPI0 + rs;
+                    float sum = 0.0f;
+#pragma unroll
+                    for (uint32_t w = 0; w < WPR; ++w) {
+                        sum += *reinterpret_cast<volatile float*>(&red[slot_i][u][warp - wr + w]);
+                    }
+                    red_count[slot_i][u][rs] = 0u;
+                    if (row < rb_end) emit(row, sum);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot_i]);  // this warp is done with the slot
+    }
+    if (aborted()) return;  // the producer warp waits for the copies in flight
+    if (p.amax) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0) warp_best[warp] = best;
+        named_bar_sync(1, kRawStagedThreads);  // the consumer warps only
+        if (tid == 0) {
+            unsigned long long b = 0ull;
+            for (uint32_t w = 0; w < NW; ++w) b = warp_best[w] > b ? warp_best[w] : b;
             if (b) atomicMax(p.amax, b);
         }
     }

@@ -145,7 +145,110 @@ cudaError_t attention_launch(const AttnParams& p, dim3 grid, cudaStream_t s, boo
     return cudaErrorInvalidValue;
 }
 
-static int raw_gemv_sms(int sms, const RawGemvParams& p, cudaStream_t s) {
+// The staged kernel for rows of up to kRawStagedMaxBlocks blocks; the
+// row-wise kernel serves wider rows, or every call under VRT_RAW_ROWWISE=1
+// (which the tests use to cover both kernels).
+using RawStagedFn = void (*)(const RawStagedParams);
+template <int U>
+static RawStagedFn raw_staged_kernel_u(uint32_t lpr) {
+    switch (lpr) {
+        case 8: return raw_gemv_staged_kernel<8, 1, U>;
+        case 16: return raw_gemv_staged_kernel<16, 1, U>;
+        case 32: return raw_gemv_staged_kernel<32, 1, U>;
+        case 64: return raw_gemv_staged_kernel<64, 1, U>;
+        case 128: return raw_gemv_staged_kernel<128, 1, U>;
+        case 256: return raw_gemv_staged_kernel<256, 1, U>;
+        case 512: return raw_gemv_staged_kernel<512, 1, U>;
+        default: return nullptr;
+    }
+}
+static RawStagedFn raw_staged_kernel_for(uint32_t lpr, uint32_t nb, uint32_t u) {
+    if (nb == 2) return lpr == 512 && u == 1 ? raw_gemv_staged_kernel<512, 2, 1> : nullptr;
+    return u == 2 ? raw_staged_kernel_u<2>(lpr) : raw_staged_kernel_u<1>(lpr);
+}
+
+static bool raw_rowwise_forced() {
+    static const bool forced = [] {
+        const char* e = getenv("VRT_RAW_ROWWISE");
+        return e && e[0] == '1';
+    }();
+    return forced;
+}
+
+// Staged launch: lanes per row LPR = the power of two >= each thread's share
+// of a row (one block per thread, two above 512 blocks), 512 / LPR row slots,
+// two rows per slot and iteration when one pass over the slots is under
+// 16 KB; ring slots of one iteration's 128-byte aligned window (plus 4 bytes
+// of read slack), as many slots as ~200 KB of shared memory holds (3..10),
+// all in flight.  CTAs are split over the matrices in proportion to their
+// rows.  Returns VRT_OK when it launched, VRT_E_UNSUPPORTED when the row-wise
+// kernel must run.
+static int raw_gemv_staged(int sms, const RawGemvParams& p, uint32_t* status, cudaStream_t s) {
+    const uint32_t nblk = p.cols / 32;
+    if (nblk == 0 || nblk > kRawStagedMaxBlocks || raw_rowwise_forced()) return VRT_E_UNSUPPORTED;
+    const uint32_t nb = nblk <= 512 ? 1 : 2;
+    const uint32_t per = (nblk + nb - 1) / nb;
+    uint32_t lpr = 8;
+    while (lpr < per) lpr *= 2;
+    const uint32_t rpi0 = kRawStagedThreads / lpr;
+    const uint64_t pass = static_cast<uint64_t>(rpi0) * nblk * 34u;
+    const uint32_t u = (nb == 1 && pass <= 16u * 1024u) ? 2 : 1;
+    const uint32_t rpi = u * rpi0;
+    const uint64_t slot =
+        ((pass * u + 2 * (kRawWindowAlign - 1) + 4 + kRawWindowAlign - 1) / kRawWindowAlign) * kRawWindowAlign;
+    const uint64_t budget = 200u * 1024u;
+    if (slot * 3 > budget) return VRT_E_UNSUPPORTED;
+    const uint32_t slots = static_cast<uint32_t>(std::min<uint64_t>(kRawStagedMaxSlots, budget / slot));
+    RawStagedParams q{};
+    q.w = p.w;
+    q.count = p.count;
+    q.cols = p.cols;
+    q.x = p.x;
+    q.y = p.y;
+    q.amax = p.amax;
+    q.status = status;
+    q.slot_bytes = static_cast<uint32_t>(slot);
+    q.slots = slots;
+    const uint64_t total = p.row_start[p.count];
+    if (total == 0) return VRT_OK;
+    uint32_t ctas = 0;
+    for (uint32_t m = 0; m < p.count; ++m) {
+        const uint32_t rows = p.row_start[m + 1] - p.row_start[m];
+        uint32_t c = static_cast<uint32_t>(static_cast<uint64_t>(sms) * rows / total);
+        c = std::max(c, rows ? 1u : 0u);
+        c = std::min(c, (rows + rpi - 1) / rpi);  // no CTA without a full iteration's worth of rows
+        q.offsets[m] = p.offsets[m];
+        q.row_start[m] = p.row_start[m];
+        q.cta_start[m] = ctas;
+        ctas += c;
+    }
+    q.row_start[p.count] = p.row_start[p.count];
+    q.cta_start[p.count] = ctas;
+    RawStagedFn k = raw_staged_kernel_for(lpr, nb, u);
+    if (!k) return VRT_E_UNSUPPORTED;
+    static std::mutex mu;
+    static uint64_t attr_done[16] = {};  // per kernel, bit d: set on device d
+    const int ai = nb == 2 ? 15 : (__builtin_ctz(lpr) - 3) + (u == 2 ? 7 : 0);
+    int dev = 0;
+    VRT_CUDA(cudaGetDevice(&dev));
+    {
+        std::lock_guard<std::mutex> g(mu);
+        const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+        if (!(attr_done[ai] & bit)) {
+            VRT_CUDA(raise_smem_limit(k));
+            attr_done[ai] |= bit;
+        }
+    }
+    VRT_CUDA(launch(k, dim3(ctas), dim3(kRawStagedThreads + 32), slots * q.slot_bytes, s, false, q));
+    return VRT_OK;
+}
+
+static int raw_gemv_sms(int sms, const RawGemvParams& p, cudaStream_t s, uint32_t* status) {
+    {
+        const int rc = raw_gemv_staged(sms, p, status, s);
+        if (rc != VRT_E_UNSUPPORTED) return rc;
+        clear_error();
+    }
     const uint32_t nblk = p.cols / 32;
     const uint32_t smem = ((nblk * 4 + 15) / 16) * 16 + p.cols * 4;
     const uint32_t rows = p.row_start[p.count];
@@ -174,8 +277,12 @@ static int raw_gemv_sms(int sms, const RawGemvParams& p, cudaStream_t s) {
     return VRT_OK;
 }
 
+// The pipeline status word of a context: the third 32-bit word of its
+// 64-byte device scratch (the first two hold the argmax key).
+static uint32_t* ctx_status_word(vrt_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->d_key) + 2; }
+
 static int raw_gemv(vrt_ctx* ctx, const RawGemvParams& p, cudaStream_t s) {
-    return raw_gemv_sms(ctx->prop.multiProcessorCount, p, s);
+    return raw_gemv_sms(ctx->prop.multiProcessorCount, p, s, ctx_status_word(ctx));
 }
 
 static int check_q8_matrix(uint64_t weights_bytes, uint64_t off, uint32_t in, uint32_t out, const char* what) {
@@ -212,6 +319,7 @@ int vrt_ctx_create(int device, vrt_ctx** out) {
     if (e == cudaSuccess) e = cudaGetDeviceProperties(&c->prop, device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&c->d_key, 64);
+    if (e == cudaSuccess) e = cudaMemset(c->d_key, 0, 64);  // argmax key + pipeline status word
     if (e != cudaSuccess) {
         delete c;
         return cuda_fail(e, "vrt_ctx_create", __FILE__, __LINE__);
@@ -413,11 +521,14 @@ int vrt_q8_ffn(vrt_ctx* ctx, const void* d_weights, uint64_t weights_bytes, uint
 // array, which every GPU that loads the library holds until the process exits.
 constexpr uint32_t kStaticFfnMax = 32768;  // largest ffn_dim accepted
 static __device__ __align__(256) float g_ffn_scratch[2 * kStaticFfnMax];
+// pipeline status word of the static entry point (kStatusWaitTimeout bits)
+static __device__ uint32_t g_static_status;
 
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
 float* g_static_ptr[kMaxDevices] = {};
+uint32_t* g_static_status_ptr[kMaxDevices] = {};
 int g_static_sms[kMaxDevices] = {};
 }  // namespace
 
@@ -426,21 +537,25 @@ int g_static_sms[kMaxDevices] = {};
 // Device address of g_ffn_scratch on the current device.  In host code the
 // array's name only stands in for the device symbol, so the address must come
 // from cudaGetSymbolAddress, once per device, with that device current.
-static int static_ffn_setup(float** ptr, int* sms) {
+static int static_ffn_setup(float** ptr, int* sms, uint32_t** status) {
     int dev = 0;
     VRT_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return fail(VRT_E_UNSUPPORTED, "device %d beyond %d", dev, kMaxDevices);
     std::lock_guard<std::mutex> g(g_static_mu);
     if (!g_static_ptr[dev]) {
         void* p = nullptr;
+        void* st = nullptr;
         VRT_CUDA(cudaGetSymbolAddress(&p, g_ffn_scratch));
+        VRT_CUDA(cudaGetSymbolAddress(&st, g_static_status));
         int n = 0;
         VRT_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
         g_static_ptr[dev] = static_cast<float*>(p);
+        g_static_status_ptr[dev] = static_cast<uint32_t*>(st);
         g_static_sms[dev] = n;
     }
     *ptr = g_static_ptr[dev];
     *sms = g_static_sms[dev];
+    if (status) *status = g_static_status_ptr[dev];
     return VRT_OK;
 }
 
@@ -462,8 +577,9 @@ int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t ga
     VRT_TRY(check_q8_matrix(weights_bytes, up_off, input_dim, ffn_dim, "Q8 fused FFN up"));
     VRT_TRY(check_q8_matrix(weights_bytes, down_off, ffn_dim, output_dim, "Q8 fused FFN down"));
     float* ws = nullptr;
+    uint32_t* status = nullptr;
     int sms = 0;
-    VRT_TRY(static_ffn_setup(&ws, &sms));
+    VRT_TRY(static_ffn_setup(&ws, &sms, &status));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // gate and up are written in full before gelu_mul reads them: the scratch
     // needs no clearing between calls
@@ -477,7 +593,7 @@ int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t ga
     p.cols = input_dim;
     p.x = d_x;
     p.y = ws;
-    VRT_TRY(raw_gemv_sms(sms, p, s));
+    VRT_TRY(raw_gemv_sms(sms, p, s, status));
     VRT_CUDA(launch(gelu_mul_kernel, dim3((ffn_dim + 255) / 256), dim3(256), 0, s, false, ws, (const float*)(ws + ffn_dim),
                     ffn_dim));
     RawGemvParams d{};
@@ -488,7 +604,25 @@ int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t ga
     d.cols = ffn_dim;
     d.x = ws;
     d.y = d_y;
-    return raw_gemv_sms(sms, d, s);
+    return raw_gemv_sms(sms, d, s, status);
+}
+
+int vrt_pipeline_status(vrt_ctx* ctx, uint32_t* h_status) {
+    clear_error();
+    if (!h_status) return fail(VRT_E_INVALID, "vrt_pipeline_status: null output");
+    uint32_t* word = nullptr;
+    if (ctx) {
+        VRT_CUDA(cudaSetDevice(ctx->device));
+        VRT_CUDA(cudaStreamSynchronize(ctx->stream));
+        word = ctx_status_word(ctx);
+    } else {
+        float* ws = nullptr;
+        int sms = 0;
+        VRT_TRY(static_ffn_setup(&ws, &sms, &word));
+    }
+    VRT_CUDA(cudaMemcpy(h_status, word, 4, cudaMemcpyDeviceToHost));
+    VRT_CUDA(cudaMemset(word, 0, 4));
+    return VRT_OK;
 }
 
 int vrt_argmax(vrt_ctx* ctx, const float* d_x, uint32_t count, vrt_argmax_result* d_out, void* stream) {

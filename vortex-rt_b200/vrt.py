@@ -94,6 +94,7 @@ _SIGS = {
     "vrt_q8_ffn": (_i, [_vp, _vp, _u64, _u64, _u64, _u64, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "vrt_q8_ffn_static": (_i, [_vp, _u64, _u64, _u64, _u64, _vp, _vp, _u32, _u32, _u32, _vp]),
     "vrt_gelu_mul": (_i, [_vp, _vp, _vp, _u32, _vp]),
+    "vrt_pipeline_status": (_i, [_vp, C.POINTER(_u32)]),
     "vrt_argmax": (_i, [_vp, _vp, _u32, _vp, _vp]),
     "vrt_lm_head_argmax": (_i, [_vp, _vp, _u64, _u64, _vp, _u32, _u32, _vp, _vp, _vp]),
     "vrt_q8t_bytes": (_u64, [_u32, _u32]),
