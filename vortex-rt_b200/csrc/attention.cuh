@@ -53,6 +53,7 @@ struct AttnParams {
     uint64_t seq_qkv, seq_cache, seq_out;
     __half* out_hi;         // when set: output as fp16 hi/lo (the o-projection
     __half* out_lo;         //   GEMM operand) instead of fp32 `out`
+    uint32_t stamp;         // timing builds: this launch's stamp slot
 };
 
 template <int M>  // M = hd / 32 values per lane
@@ -116,6 +117,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
 
     pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) chain_stamp(p.stamp, 0);
+    ChainStampEnd stamp_end{p.stamp, tid == 0};
     const uint32_t g = blockIdx.y, s = blockIdx.x, z = BATCH ? blockIdx.z : 0u;
     // this sequence's pointers (z = 0 and zero strides for a single sequence)
     const uint64_t zz = z;
@@ -134,6 +137,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
     // not even the position: under programmatic launch the previous step's
     // finalize may still be in flight when this grid starts.
     pdl_wait();
+    if (tid == 0) {
+        chain_stamp(p.stamp, 1);
+        chain_stamp(p.stamp, 2);
+    }
     const uint32_t pos = p.pos[z];
     const uint32_t n = p.window ? min(pos + 1, p.window) : pos + 1;
     const uint32_t first = pos + 1 - n;  // oldest position attended
@@ -193,6 +200,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
         }
     }
     __syncthreads();
+    if (tid == 0) chain_stamp(p.stamp, 4);
 
     // 3. online softmax, P positions per warp step
     float mx[RG], sm[RG], acc[RG][M];

@@ -59,6 +59,7 @@ struct GemvParams {
     // Resid*: tensor-parallel exchange of the block output (tp.world > 1);
     // x then points at tp.sum, which this launch fills before its prologue.
     TpParams tp;
+    uint32_t stamp;              // timing builds: this launch's stamp slot
 };
 
 // First tile of CTA b's span under the partition rule of the kernel below.
@@ -262,6 +263,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
     float* xs = reinterpret_cast<float*>(smem + L.xs);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) chain_stamp(p.stamp, 0);
+    ChainStampEnd stamp_end{p.stamp, tid == 0};
     const uint32_t kt = p.cols / kTileCols;
     const uint32_t n_groups = (p.rows + kTileRows - 1) / kTileRows;
     uint64_t T0, T1;
@@ -311,6 +314,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
 
     // --------------------------------------------------------- consumers
     pdl_wait();
+    if (tid == 0) {
+        chain_stamp(p.stamp, 1);
+        chain_stamp(p.stamp, 2);
+    }
     const int ctid = tid;  // 0..255
     constexpr int NC = kConsumerWarps * 32;
     if (p.zero0) {
@@ -336,6 +343,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
             named_bar_sync(1, NC);
             if (ctid == 0) tp_grid_barrier(p.tp, seq, p.status);
             named_bar_sync(1, NC);
+            if (ctid == 0) chain_stamp(p.stamp, 3);
         }
     }
 
@@ -414,6 +422,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
         for (uint32_t blk = ctid; blk < nblk; blk += NC) quant_block(xs + blk * 32, blk, x16p, sx);
     }
     named_bar_sync(1, NC);
+    if (ctid == 0) chain_stamp(p.stamp, 4);
 
     // ------------------------------------------------------- main loop
     const uint32_t g_first = static_cast<uint32_t>(T0 / kt);

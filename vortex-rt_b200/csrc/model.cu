@@ -1100,6 +1100,7 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
         p.next_grid = static_cast<uint32_t>(gemv_grid(sms, nx.rows));
         p.next_group = nx.group ? 1u : 0u;
         p.pf_bytes = 64u * 1024u;
+        p.stamp = nk;
         ++gi;
         VRT_CUDA(gemv_q8t(pro, epi, p, gemv_grid(sms, p.rows), s, pdl));
         ++nk;
@@ -1156,6 +1157,7 @@ static int record_step(vrt_model* m, cudaStream_t s, bool head, uint32_t* kernel
             a.splits = L.splits;
             a.zero0 = m->dn;
             a.zero0_count = d;
+            a.stamp = nk;
             VRT_CUDA(attention_launch(a, dim3(L.splits, m->KVl), s, pdl));
             ++nk;
         }

@@ -607,6 +607,21 @@ int vrt_q8_ffn_static(const void* d_weights, uint64_t weights_bytes, uint64_t ga
     return raw_gemv_sms(sms, d, s, status);
 }
 
+#ifdef VRT_CHAIN_STAMPS
+// Timing builds only: copy the first n launch slots of the decode-step stamps
+// ([n][6] globaltimer values, see chain_stamp) to the host and reset them.
+__attribute__((visibility("default"))) int vrt_chain_stamps(unsigned long long* h_out, uint32_t n) {
+    if (n > kChainStampSlots) n = kChainStampSlots;
+    VRT_CUDA(cudaDeviceSynchronize());
+    VRT_CUDA(cudaMemcpyFromSymbol(h_out, g_chain_stamps, sizeof(unsigned long long) * kChainStampFields * n));
+    static unsigned long long init[kChainStampSlots][kChainStampFields];
+    for (uint32_t i = 0; i < kChainStampSlots; ++i)
+        for (int f = 0; f < kChainStampFields; ++f) init[i][f] = f <= 1 ? ~0ull : 0ull;
+    VRT_CUDA(cudaMemcpyToSymbol(g_chain_stamps, init, sizeof(init)));
+    return VRT_OK;
+}
+#endif
+
 int vrt_pipeline_status(vrt_ctx* ctx, uint32_t* h_status) {
     clear_error();
     if (!h_status) return fail(VRT_E_INVALID, "vrt_pipeline_status: null output");

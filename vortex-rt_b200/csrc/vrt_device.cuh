@@ -144,6 +144,44 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// ------------------------------------------------------- timing builds
+// An instrumented build (`make stamps`: -DVRT_CHAIN_STAMPS, never the
+// default) records per decode-step launch `slot` the globaltimer at phase
+// boundaries, reduced over the launch's CTAs: [0] first CTA start (min),
+// [1] first wait release (min), [2] last wait release (max), [3] last CTA past
+// the tensor-parallel exchange (max), [4] last CTA past its prologue (max),
+// [5] last CTA end (max).  One thread per CTA stamps.  In the default build
+// every call compiles to nothing.
+constexpr uint32_t kChainStampSlots = 2048;
+constexpr int kChainStampFields = 6;
+#ifdef VRT_CHAIN_STAMPS
+static __device__ unsigned long long g_chain_stamps[kChainStampSlots][kChainStampFields];
+#endif
+__device__ __forceinline__ void chain_stamp(uint32_t slot, int field) {
+#ifdef VRT_CHAIN_STAMPS
+    if (slot >= kChainStampSlots) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (field <= 1) {
+        atomicMin(&g_chain_stamps[slot][field], t);
+    } else {
+        atomicMax(&g_chain_stamps[slot][field], t);
+    }
+#else
+    (void)slot;
+    (void)field;
+#endif
+}
+// Stamps field 5 (end) when the CTA's stamping thread leaves the kernel, on
+// every return path.
+struct ChainStampEnd {
+    uint32_t slot;
+    bool on;
+    __device__ ~ChainStampEnd() {
+        if (on) chain_stamp(slot, 5);
+    }
+};
+
 // ------------------------------------------------------------- numerics
 
 // Device status bits (vrt_model_device_status).

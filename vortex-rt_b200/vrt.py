@@ -18,7 +18,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-LIB_PATH = os.path.join(HERE, "libvortexrt_b200.so")
+# VRT_LIB: another build of the library (e.g. the timing build of `make stamps`)
+LIB_PATH = os.environ.get("VRT_LIB") or os.path.join(HERE, "libvortexrt_b200.so")
 HEADER = os.path.join(ROOT, "include", "vortexrt_b200.h")
 
 VRT_OK, VRT_E_INVALID, VRT_E_CUDA, VRT_E_NOMEM, VRT_E_IO, VRT_E_STATE, VRT_E_NUMERIC, VRT_E_TIMEOUT, \
