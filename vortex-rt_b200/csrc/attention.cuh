@@ -141,6 +141,25 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
         chain_stamp(p.stamp, 1);
         chain_stamp(p.stamp, 2);
     }
+    // Loads that do not depend on the position go out with it, in one round:
+    // this warp's first query row and, for the last warp (which handles the
+    // newest key/value), this KV head's new k and v.
+    constexpr uint32_t kKvWarp = kAttnWarps - 1;
+    float q_first[M], k_new[M], v_new[M];
+    if (static_cast<uint32_t>(warp) < R) {
+        const float* src = qkv + static_cast<uint64_t>(g * R + warp) * hd;
+#pragma unroll
+        for (int m = 0; m < M; ++m) q_first[m] = src[lane + 32 * m];
+    }
+    if (warp == kKvWarp) {
+        const float* ks = qkv + static_cast<uint64_t>(p.H) * hd + static_cast<uint64_t>(g) * hd;
+        const float* vs = qkv + static_cast<uint64_t>(p.H + p.KV) * hd + static_cast<uint64_t>(g) * hd;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            k_new[m] = ks[lane + 32 * m];
+            v_new[m] = vs[lane + 32 * m];
+        }
+    }
     const uint32_t pos = p.pos[z];
     const uint32_t n = p.window ? min(pos + 1, p.window) : pos + 1;
     const uint32_t first = pos + 1 - n;  // oldest position attended
@@ -170,33 +189,32 @@ __global__ void __launch_bounds__(kAttnThreads) attention_decode_kernel(const At
 
     // 1. queries
     for (uint32_t r = warp; r < R; r += kAttnWarps) {
-        const float* src = qkv + static_cast<uint64_t>(g * R + r) * hd;
         float v[M];
+        if (r == static_cast<uint32_t>(warp)) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) v[m] = src[lane + 32 * m];
+            for (int m = 0; m < M; ++m) v[m] = q_first[m];
+        } else {
+            const float* src = qkv + static_cast<uint64_t>(g * R + r) * hd;
+#pragma unroll
+            for (int m = 0; m < M; ++m) v[m] = src[lane + 32 * m];
+        }
         head_norm_rope<M>(v, p.q_norm, cs, sn, hd, p.eps, lane);
 #pragma unroll
         for (int m = 0; m < M; ++m) q_s[r][lane + 32 * m] = v[m];
     }
     // 2. the newest key/value
     const bool has_new = t0 < t1 && t1 == pos + 1;
-    if (has_new && warp == 0) {
-        const float* ks = qkv + static_cast<uint64_t>(p.H) * hd + static_cast<uint64_t>(g) * hd;
-        const float* vs = qkv + static_cast<uint64_t>(p.H + p.KV) * hd + static_cast<uint64_t>(g) * hd;
-        float v[M];
-#pragma unroll
-        for (int m = 0; m < M; ++m) v[m] = ks[lane + 32 * m];
-        head_norm_rope<M>(v, p.k_norm, cs, sn, hd, p.eps, lane);
+    if (has_new && warp == kKvWarp) {
+        head_norm_rope<M>(k_new, p.k_norm, cs, sn, hd, p.eps, lane);
         const uint32_t slot = pos % p.cap;
         float* kd = k_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
         float* vd = v_cache + (static_cast<uint64_t>(g) * p.cap + slot) * hd;
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-            const float vv = vs[lane + 32 * m];
-            knew[lane + 32 * m] = v[m];
-            vnew[lane + 32 * m] = vv;
-            kd[lane + 32 * m] = v[m];
-            vd[lane + 32 * m] = vv;
+            knew[lane + 32 * m] = k_new[m];
+            vnew[lane + 32 * m] = v_new[m];
+            kd[lane + 32 * m] = k_new[m];
+            vd[lane + 32 * m] = v_new[m];
         }
     }
     __syncthreads();
