@@ -883,7 +883,7 @@ def batched_run(args, workload: str, rank: int, world: int, local: int, dist_on:
     line = {
         "metric": METRIC.replace("bs=1", f"batched, {total} sequences"), "value": tok_s, "unit": "tok/s",
         "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
-        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "q8_0*int8/fp16->f32",
         "data": "synthetic (seeded Q8_0 weights generated on device, seeded uniform prompt ids)",
         "config": {"workload": {"270m-batch": f"config 3: 270M-shaped Gemma 3 Q8_0, {total} sequences x "
