@@ -166,6 +166,28 @@ __device__ __forceinline__ void quant_block(const float* v, uint32_t blk, int16_
     }
 }
 
+// The same quantisation spread over 8 threads per block: thread t8 = 0..7 of
+// block blk holds elements 4*t8..4*t8+3 in v.  The block maximum is taken
+// with fmaxf from 0 (exact in any order, NaN never wins), so the digits and
+// the scale equal quant_block's.  All 32 lanes of the warp must call it
+// (shuffles); `valid` is uniform over each aligned group of 8 lanes.
+__device__ __forceinline__ void quant_block8(const float4 v, uint32_t blk, uint32_t t8, bool valid, int16_t* x16p,
+                                             float* sx) {
+    float amax = fmaxf(fmaxf(fmaxf(fmaxf(0.0f, fabsf(v.x)), fabsf(v.y)), fabsf(v.z)), fabsf(v.w));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    if (!valid) return;
+    const float s = quant_scale(amax);
+    const float inv = amax > 0.0f ? 32767.0f / amax : 0.0f;
+    if (t8 == 0) sx[blk] = s;
+    const uint32_t base = (blk / 4) * 128 + (blk % 4) * 8 + (t8 / 2) * 32 + (t8 % 2) * 4;
+    const int q0 = quant_one(v.x, inv), q1 = quant_one(v.y, inv), q2 = quant_one(v.z, inv), q3 = quant_one(v.w, inv);
+    *reinterpret_cast<uint2*>(x16p + base) =
+        make_uint2((static_cast<uint32_t>(q0) & 0xffffu) | (static_cast<uint32_t>(q1) << 16),
+                   (static_cast<uint32_t>(q2) & 0xffffu) | (static_cast<uint32_t>(q3) << 16));
+}
+
 // Prologue helper for the norm modes: every consumer thread holds up to
 // kPrologueVec float4 of each input vector in registers, loaded in one round
 // trip; returns x (the activation to quantise) in xs[] (shared, fp32).
@@ -348,7 +370,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
     }
 
     const uint32_t K = p.cols, nblk = K / 32;
-    if (PRO == kProPlain) {
+    if (PRO == kProPlain && nblk * 8 <= 3 * NC) {
+        // short vectors: 8 threads per block, coalesced float4 loads, all in flight at once
+        const float4* x4 = reinterpret_cast<const float4*>(p.x);
+        float4 f[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            const uint32_t i = ctid + r * NC;
+            f[r] = i < nblk * 8 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            const uint32_t i = ctid + r * NC;
+            quant_block8(f[r], i / 8, i % 8, i < nblk * 8, x16p, sx);
+        }
+    } else if (PRO == kProPlain) {
         // blocks of 32 activations: all loads of a thread issued before use
         for (uint32_t b0 = 0; b0 < nblk; b0 += 3 * NC) {
             float4 f[3][8];
@@ -419,7 +455,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q8t_gemv_kernel(const GemvPar
             }
         }
         named_bar_sync(1, NC);
-        for (uint32_t blk = ctid; blk < nblk; blk += NC) quant_block(xs + blk * 32, blk, x16p, sx);
+        if (nblk * 8 <= 2 * NC) {  // short vectors: 8 threads per block
+            const float4* xs4 = reinterpret_cast<const float4*>(xs);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint32_t i = ctid + r * NC;
+                const bool ok = i < nblk * 8;
+                quant_block8(ok ? xs4[i] : make_float4(0.f, 0.f, 0.f, 0.f), i / 8, i % 8, ok, x16p, sx);
+            }
+        } else {
+            for (uint32_t blk = ctid; blk < nblk; blk += NC) quant_block(xs + blk * 32, blk, x16p, sx);
+        }
     }
     named_bar_sync(1, NC);
     if (ctid == 0) chain_stamp(p.stamp, 4);
